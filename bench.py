@@ -1,0 +1,358 @@
+"""Benchmark: Sinkhorn ms per iteration (one f half-step + one g half-step) on the fused CUDA half-step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload auto|cfg2|cfg5|weak]
+
+Workloads (synthetic, seeded; trnopt.synthetic):
+  cfg2  n = m = 10,000, d = 64, x, y ~ U[0,1]^64, eps 0.1, raw cost (the N = 1 default)
+  weak  the N > 1 default: n = 10,000 N rows, m = 10,000, d = 64 (config 2's per-GPU work at every N)
+  cfg5  n = m = 262,144, d = 64, x, y ~ N(0, I)/8, mean-normalised cost, eps 0.01 (strong
+        scaling over N)
+A step is one Sinkhorn iteration with the inputs resident in HBM; L2 (126 MB) is flushed between timed steps by
+writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU, rows of every
+half-step are split across the ranks and the new potential is all-gathered with NCCL; the reported time is the
+max over ranks.
+
+--impl reference times the reference's CPU solver on this host's cores (the CPU port in oracle/, float32, all
+threads) on the same workload; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "trainium-sinkhorn_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "Sinkhorn ms/iter (10k^2 d=64; 262k^2 d=64 @1/2/4/8 B200)"
+SMS = 148
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak"])
+    ap.add_argument("--path", default="auto", choices=["auto", "ffma", "tc"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-flush", action="store_true", help="(profiling runs only) do not flush L2 between steps")
+    return ap.parse_args()
+
+
+def workload(name: str, world: int):
+    from trnopt import synthetic
+    if name == "auto":
+        name = "cfg2" if world == 1 else "weak"
+    if name == "cfg2":
+        x, y = synthetic.cfg2()
+        return name, x, y, dict(eps=0.1, normalize=False), {"n": 10_000, "m": 10_000, "d": 64, "eps": 0.1}
+    if name == "weak":
+        x, y = synthetic.cfg2(n=10_000 * world)
+        return name, x, y, dict(eps=0.1, normalize=False), {"n": 10_000 * world, "m": 10_000, "d": 64, "eps": 0.1}
+    x, y = synthetic.cfg5()
+    return name, x, y, dict(eps=0.01, normalize="mean"), {"n": len(x), "m": len(y), "d": 64, "eps": 0.01}
+
+
+class Clocks:
+    """nvidia-smi samples of this GPU's SM clock and throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int, enabled: bool):
+        self.proc, self.lines, self.enabled = None, [], enabled
+        self.target = None
+        try:
+            self.target = str(torch.cuda.get_device_properties(dev).uuid)
+            if not self.target.startswith("GPU-"):
+                self.target = "GPU-" + self.target
+        except Exception:
+            self.target = None
+
+    def __enter__(self):
+        if self.enabled:
+            cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200"]
+            if self.target:
+                cmd += ["-i", self.target]
+            try:
+                self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.reader = threading.Thread(target=self._read, daemon=True)
+                self.reader.start()
+            except OSError:
+                self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [s.strip() for s in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_oracle_iteration_ms(x, y, kw, max_seconds: float, threads: int | None = None):
+    """The reference's CPU solver (oracle port, torch float32, all threads) on a bounded sample of the workload:
+    whole iterations when they fit the time budget, else the f and g half-steps over a subset of rows, scaled."""
+    from oracle import trnopt_oracle as O
+    torch.set_num_threads(threads or os.cpu_count() or 1)
+    eps = kw["eps"]
+    if kw["normalize"]:
+        center, scale = O.normalization(x, y, how="mean")
+    else:
+        center, scale = np.zeros(x.shape[1]), 1.0
+    xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
+    n, m = len(xs), len(ys)
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32)
+    X, Y = t(xs), t(ys)
+    XT, YT = X.T.contiguous(), Y.T.contiguous()
+    xsq, ysq = t((xs * xs).sum(1)), t((ys * ys).sum(1))
+    la, lb = torch.full((n,), float(-np.log(n))), torch.full((m,), float(-np.log(m)))
+    zx, zy = torch.zeros(n), torch.zeros(m)
+    gh = torch.zeros(m)
+    inv, e, k = (torch.tensor(v, dtype=torch.float32) for v in (1.0 / eps, eps, 1.0))
+
+    blk = max(n, m) if n * m <= 150_000_000 else 4096   # the reference's default block=None where it fits
+
+    def iteration(rows_x, rows_y):
+        fh = torch.cat([O.half_step(X[s:s + blk], xsq[s:s + blk], zx[s:s + blk], YT, gh, lb, inv, e, k)
+                        for s in range(0, rows_x, blk)])
+        gg = torch.cat([O.half_step(Y[s:s + blk], ysq[s:s + blk], zy[s:s + blk], XT, fh if rows_x == n else zx, la,
+                                    inv, e, k) for s in range(0, rows_y, blk)])
+        return gg
+
+    t0 = time.perf_counter()
+    iteration(min(n, 4096), min(m, 4096))                     # warm-up on one block of rows each way
+    t_blk = time.perf_counter() - t0
+    est_full = t_blk * (n / min(n, 4096) + m / min(m, 4096)) / 2
+    if est_full * 2 <= max_seconds:
+        reps, frac = 2, 1.0
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            iteration(n, m)
+        dt = (time.perf_counter() - t0) / reps
+        sample = f"{reps} full iterations ({n}x{m}, d {x.shape[1]}) after a 4096-row warm-up"
+    else:
+        frac = max(4096 / max(n, m), min(1.0, max_seconds / (2 * est_full)))
+        rx, ry = max(1, int(n * frac)), max(1, int(m * frac))
+        t0 = time.perf_counter()
+        iteration(rx, ry)
+        dt = (time.perf_counter() - t0) * (n + m) / (rx + ry)
+        sample = f"f and g half-steps over {rx} + {ry} of {n} + {m} rows, scaled to a full iteration"
+    return dt * 1e3, torch.get_num_threads(), sample
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    name, x, y, kw, cfg = workload(args.workload, world)
+    budget_per_step = max(0.5, 150.0 / max(1, args.steps + args.warmup))
+    # Each step is one bounded sample of an iteration, timed on the host's cores.
+    vals, cores, sample = [], 0, ""
+    for i in range(args.warmup + args.steps):
+        ms, cores, sample = cpu_oracle_iteration_ms(x, y, kw, budget_per_step)
+        if i >= args.warmup:
+            vals.append(ms)
+    v = float(np.mean(vals))
+    line = {"metric": METRIC, "value": v, "unit": "ms/iter", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False, "scaling": "weak" if name == "weak"
+            else "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": name, **cfg, "l2": "inputs resident in host memory"},
+            "cpu_baseline": {"value": v, "unit": "ms/iter", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "ms/iter", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, dev):
+    import trnopt.sinkhorn  # noqa: F401
+    from trnopt import Backend, SinkhornOptions, _capi, sinkhorn
+    S = sys.modules["trnopt.sinkhorn"]
+    name, x, y, kw, cfg = workload(args.workload, world)
+    eps = kw["eps"]
+    path = S._resolve_path(args.path, x.shape[1]) if hasattr(S, "_resolve_path") else "ffma"
+    if kw["normalize"]:
+        center, scale = S.normalization(x, y, how="mean")
+    else:
+        center, scale = np.zeros(x.shape[1]), 1.0
+    xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
+    shift = np.concatenate([xs, ys]).mean(axis=0)
+    xi, yi = xs - shift, ys - shift
+    n, m = len(x), len(y)
+    la, lb = np.full(n, -np.log(n)), np.full(m, -np.log(m))
+    X = S._Cloud(xi, la, world, dev)
+    Y = S._Cloud(yi, lb, world, dev)
+    if hasattr(S, "_prepare_path"):
+        S._prepare_path(path, X, Y)
+    ws = S._workspace(X, Y, world, dev, path) if path != "ffma" else S._workspace(X, Y, world, dev)
+    step = S._CudaStep(dev, world, rank, ws, path=path) if path != "ffma" else S._CudaStep(dev, world, rank, ws)
+    gh = torch.zeros(Y.npad, dtype=torch.float32, device=dev)
+    fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def iteration(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        step(X, Y, gh, eps, 1.0, out=fh)
+        if ev is not None:
+            ev[1].record(stream)
+        step(Y, X, fh, eps, 1.0, out=gh)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        iteration()
+    torch.cuda.synchronize(dev)
+    steps = []
+    with Clocks(dev.index, enabled=not args.no_clocks and rank == 0) as clk:
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        for _ in range(args.steps):
+            if not args.no_flush:
+                flush.zero_()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            iteration(ev)
+            steps.append(ev)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+    step_ms = [a.elapsed_time(c) for a, _, c in steps]
+    f_ms = [a.elapsed_time(b) for a, b, _ in steps]
+    g_ms = [b.elapsed_time(c) for _, b, c in steps]
+    total = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(total, op=torch.distributed.ReduceOp.MAX)
+    ms_per_step = float(total.item()) / args.steps
+    clocks = clk.summary() if rank == 0 else None
+    if _capi.device_error_flags():
+        raise RuntimeError("a kernel reported device error flags during the timed region")
+
+    # Roofline of the dominant kernel (the fused half-step): per launch, useful FLOPs 2 rows m d, exps rows m.
+    rows_f, rows_g = X.npad // world, Y.npad // world
+    launch_ms = (statistics.mean(f_ms) + statistics.mean(g_ms)) / 2
+    flops = (2.0 * rows_f * Y.npad * X.d + 2.0 * rows_g * X.npad * X.d) / 2
+    exps = (rows_f * Y.npad + rows_g * X.npad) / 2.0
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    peak_src = "measured" if peaks else "fallback"
+    mhz = (clocks or {}).get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    tflops = flops / (launch_ms * 1e-3) / 1e12
+    ffma_peak = SMS * 128 * 2 * mhz * 1e6 / 1e12
+    sfu_rate = exps / (launch_ms * 1e-3)
+    sfu_peak = SMS * 16 * mhz * 1e6
+    traffic = None
+    tfile = ROOT / "profiles" / f"traffic_{path}_{name}.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+    roof = {"bound": "tensor", "achieved": round(tflops, 2), "peak": bf16, "unit": "TFLOP/s",
+            "frac": round(tflops / bf16, 4), "traffic": traffic, "peak_source": peak_src,
+            "kernel": f"half-step ({path})", "launch_ms": round(launch_ms, 5),
+            "sfu": {"achieved_exp_per_s": sfu_rate, "peak_exp_per_s": sfu_peak, "frac": round(sfu_rate / sfu_peak, 4),
+                    "clock_mhz": mhz},
+            "ffma": {"achieved_tflops": round(tflops, 2), "peak_tflops": round(ffma_peak, 2),
+                     "frac": round(tflops / ffma_peak, 4)}}
+
+    # End to end through the public API: host arrays in, potentials out, K iterations.
+    e2e = None
+    if not args.no_e2e:
+        opts = SinkhornOptions(max_iters=args.steps, fixed_iters=True, backend=Backend.preset("cuda-fused", device=str(dev)),
+                               cores=world, **({"cuda_path": path} if path != "ffma" else {}), **kw)
+        sinkhorn(x[:256], y[:256], opts=SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend,
+                                                         cores=world, **kw))
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        r = sinkhorn(x, y, opts=opts)
+        torch.cuda.synchronize(dev)
+        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(dt, op=torch.distributed.ReduceOp.MAX)
+        h2d = X.h2d_bytes + Y.h2d_bytes + 4 * Y.npad
+        d2h = 8 * (n + m) // 2
+        e2e = {"value": float(dt.item()) * 1e3 / r.iterations, "unit": "ms/iter",
+               "h2d_bytes_per_step": h2d / r.iterations, "d2h_bytes_per_step": 4 * (n + m) / r.iterations,
+               "note": "one public sinkhorn() call on host float64 arrays (upload, normalisation, padding, "
+                       f"{r.iterations} fixed iterations, f and g back to the host), divided by the iterations"}
+        del d2h
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ms, cores, sample = cpu_oracle_iteration_ms(x, y, kw, 20.0)
+        cpu = {"value": ms, "unit": "ms/iter", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": ms_per_step, "unit": "ms/iter", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": False,
+                "scaling": "strong" if name in ("cfg2", "cfg5") else "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded generators in trnopt.synthetic)",
+                "config": {"workload": name, **cfg, "path": path, "shards": world,
+                           "l2": "flushed between timed steps (256 MB write)"},
+                "gpu_launches": 2 * args.steps, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 needs torchrun --nproc-per-node N")
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world, dev)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

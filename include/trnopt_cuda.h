@@ -1,0 +1,103 @@
+/* trnopt_cuda.h -- C ABI of the B200 (sm_100a) fused log-domain Sinkhorn half-step library (libtrnopt_cuda.so).
+ *
+ * This library replaces the hot path of trnopt (evandiewald/trainium-sinkhorn): the half-step
+ *     fh_i = kappa * (|x_i|^2 + eps * off_i - eps * lse_i) - |x_i|^2,
+ *     lse_i = log sum_j exp( (2 x_i . y_j + gh_j) / eps + log b_j )
+ * of src/trnopt/sinkhorn.py:108-119 (the PyTorch _half_step) and src/trnopt/nki_sinkhorn.py:175-228 (the fused
+ * NKI kernel), plus the companions around it in the solver loop.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. Every array pointer is a DEVICE pointer on the calling thread's current CUDA
+ *     device; `stream` is a cudaStream_t (NULL = the legacy default stream). Calls are asynchronous on `stream`
+ *     unless stated otherwise.
+ *   - Point clouds are passed transposed, as the reference's kernel takes them (xa_T / yT in
+ *     nki_sinkhorn.py:175-182): xT[k * ldx + i] is coordinate k of point i. ldx >= rows, ldx % 4 == 0, and xT,
+ *     yT are 16-byte aligned. All floating-point arrays are float32.
+ *   - Every entry point returns TRNOPT_OK (0) or a negative status; trnopt_status_string() names it. Nothing
+ *     is launched when an argument check fails.
+ *   - The caller owns all memory. The library never allocates device memory on these paths and never frees
+ *     caller memory. Scratch space is a caller-provided workspace (see trnopt_workspace_size).
+ */
+#ifndef TRNOPT_CUDA_H_
+#define TRNOPT_CUDA_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TRNOPT_OK = 0,
+  TRNOPT_ERR_INVALID_ARGUMENT = -1, /* a size, scalar or null pointer is out of range */
+  TRNOPT_ERR_ALIGNMENT = -2,        /* a pointer or leading dimension breaks the alignment rules above */
+  TRNOPT_ERR_WORKSPACE = -3,        /* workspace missing or smaller than trnopt_workspace_size() */
+  TRNOPT_ERR_UNSUPPORTED = -4,      /* shape or path not supported on this build / device */
+  TRNOPT_ERR_CUDA = -5,             /* a CUDA runtime call failed (trnopt_last_cuda_error() has the code) */
+  TRNOPT_ERR_DEVICE = -6            /* a kernel reported an error flag (see trnopt_device_error_flags) */
+};
+
+enum { TRNOPT_PATH_FFMA = 0, TRNOPT_PATH_TC = 1 };
+
+/* Library version, e.g. 100 for 0.1.0. No reference counterpart. */
+int trnopt_version(void);
+
+/* Human-readable name of a status code. */
+const char* trnopt_status_string(int status);
+
+/* The cudaError_t of the last failed CUDA call made by this library on the calling thread (0 if none). */
+int trnopt_last_cuda_error(void);
+
+/* Synchronises `stream`, then reads and clears the device error word of the current device: bit 1 = a bounded
+ * wait inside a kernel gave up, bit 2 = tensor-memory allocation gave up, bit 4 = a launch invariant failed.
+ * The reference has no device-side errors; its failures are Python exceptions (sinkhorn.py:201-207). */
+int trnopt_device_error_flags(void* stream, int* flags_out);
+
+/* Bytes of workspace that trnopt_half_step / trnopt_row_lse (path FFMA) or trnopt_half_step_tc (path TC) need
+ * for `rows` x `m` on the current device. The workspace holds per-row partial (max, sum) pairs of split rows and
+ * one arrival counter per 128-row tile. Replaces the reference's per-call intermediates (the dense score tile
+ * of sinkhorn.py:116, the on-chip per-chunk statistics of nki_sinkhorn.py:87-96). */
+size_t trnopt_workspace_size(int rows, int m, int d, int path);
+
+/* Zero a workspace once after allocating it. The kernels leave it zeroed again when they finish, so one init
+ * serves any number of calls on one stream; calls that overlap on the GPU must use separate workspaces. */
+int trnopt_workspace_init(void* workspace, size_t ws_bytes, void* stream);
+
+/* The fused half-step, FP32 FFMA tile path. Replaces _half_step (sinkhorn.py:108-119) and the NKI kernel
+ * make_half_step_kernel(d, rows, m)(xa_T, xsq, off, yT, gh, log_b, sc) (nki_sinkhorn.py:175-228):
+ *   xT (d, ldx)  rows of this side, transposed        xsq (rows,)  |x_i|^2
+ *   off (rows,)  log(target / reference) or NULL (= 0) yT (d, ldy)  the other side, transposed
+ *   gh (m,)      shifted potential of the other side    log_b (m,)   log weights of the other side
+ *   eps, kappa   the scalars of sc = [2/eps, 1/eps, eps, kappa] (sinkhorn.py:331-333)
+ *   fh (rows,)   output: the new shifted potential
+ * 1 <= d <= 128. Padding columns carry log_b = -1e9 exactly as in the reference (sinkhorn.py:59,144). */
+int trnopt_half_step(const float* xT, int ldx, const float* xsq, const float* off, const float* yT, int ldy,
+                     const float* gh, const float* log_b, int rows, int m, int d, float eps, float kappa,
+                     float* fh, void* workspace, size_t ws_bytes, void* stream);
+
+/* Row log-sum-exp of a product, lse_i = log sum_j exp(xa_i . ya_j), xa_T (k, ldx), ya_T (k, ldy), 1 <= k <= 128.
+ * Replaces make_row_lse_kernel(K, rows, m)(xa_T, ya_T) (nki_sinkhorn.py:150-172). */
+int trnopt_row_lse(const float* xaT, int ldx, const float* yaT, int ldy, int rows, int m, int k, float* lse,
+                   void* workspace, size_t ws_bytes, void* stream);
+
+/* Convergence checks of the solver loop (sinkhorn.py:358-374), reduced on the device into out[0]:
+ *   balanced:   sum_j | w_j (exp(min((gh_old_j - gh_new_j) * inv_eps, 50)) - 1) |   (sinkhorn.py:370-371)
+ *   max change: max_j |gh_new_j - gh_old_j| * inv_eps over j < n                    (sinkhorn.py:360, 373) */
+int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float* w, int n, float inv_eps,
+                          float* out, void* stream);
+int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream);
+
+/* Exact median of all n m clamped costs max(C_ij, 0), C_ij = (sqx_i + sqy_j) - 2 xc_i . yc_j, float64, written to
+ * out[0]; the mean of the two middle values when n m is even (np.median). xc (n, d) and yc (m, d) are row-major
+ * centred points, sqx / sqy their squared norms. n m <= 1e8, d <= 128. Replaces the host NumPy median of
+ * normalization(how="median") (sinkhorn.py:229-233). The costs are re-evaluated in 16 passes and never stored;
+ * the workspace (trnopt_median_workspace_size bytes, 256-byte aligned) needs no initialisation. */
+size_t trnopt_median_workspace_size(void);
+int trnopt_median_cost(const double* xc, const double* yc, const double* sqx, const double* sqy, int n, int m, int d,
+                       double* out, void* workspace, size_t ws_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRNOPT_CUDA_H_ */

@@ -1,0 +1,184 @@
+"""Generate the golden fixtures in this folder by running the reference trnopt (pure Python/PyTorch) on the CPU.
+
+    TRNOPT_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden.py
+
+The reference is importable only in the build container; the fixtures it writes are committed so that tests on
+any machine (the GPU box included) compare against the reference's own outputs without needing it. Inputs are
+stored beside outputs, or regenerated from the seeded generators in trnopt.synthetic.
+
+Files:
+  half_step_kat.npz     reference _half_step (sinkhorn.py:108-119) in float64 and float32 on random blocks with
+                        padded columns, off != 0 and kappa < 1, d in {5, 16, 30, 64}
+  row_lse_kat.npz       the row-LSE known-answer inputs of examples/nki_sinkhorn_check.py:22-35 and the float64
+                        answer (scipy logsumexp of xa^T ya)
+  solver_cases.npz      reference sinkhorn() on the cases of tests/test_sinkhorn.py (fp64 and fp32)
+  cfg1.npz              config 1 (2,000^2, d 16, 200 fixed iterations, eps 0.1, raw cost): f, g in fp64 and fp32,
+                        and the fp64 plan's row / column sums
+  normalization.npz     normalization() scales (mean and median, odd and even n m, config 3's full pair)
+  wot_small.npz         wot_transport_map() on a reduced config-3 pair (fp64, 3 growth iterations)
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, os.environ.get("TRNOPT_REFERENCE_SRC", "/root/reference/src"))
+from trnopt import Backend  # noqa: E402  (the reference)
+import trnopt.sinkhorn  # noqa: E402,F401
+
+ref_sk = sys.modules["trnopt.sinkhorn"]   # the module (the package attribute of that name is the function)
+from trnopt.singlecell import wot_transport_map  # noqa: E402
+
+sys.path.insert(0, str(ROOT / "trainium-sinkhorn_b200"))
+import importlib.util  # noqa: E402
+
+_spec = importlib.util.spec_from_file_location("_synthetic", ROOT / "trainium-sinkhorn_b200/trnopt/synthetic.py")
+synthetic = importlib.util.module_from_spec(_spec)
+sys.modules["_synthetic"] = synthetic
+_spec.loader.exec_module(synthetic)
+
+torch.set_num_threads(os.cpu_count() or 1)
+CPU64, CPU32 = Backend.preset("cpu"), Backend.preset("cpu-float32")
+
+
+def clouds(n=137, m=91, d=5, seed=0):
+    """The reference test suite's clouds (tests/test_sinkhorn.py:47-51)."""
+    rng = np.random.default_rng(seed)
+    return rng.normal(size=(n, d)), rng.normal(size=(m, d)) * 0.8 + 0.5
+
+
+def half_step_kat():
+    out = {}
+    cases = [(0, 5, 150, 333, 0.1, 1.0), (1, 16, 200, 500, 0.05, 0.9), (2, 30, 129, 257, 0.05, 0.98),
+             (3, 64, 160, 300, 0.1, 1.0), (4, 64, 96, 1100, 0.02, 0.7)]
+    for cid, d, k, m, eps, kappa in cases:
+        rng = np.random.default_rng(100 + cid)
+        x = rng.normal(size=(k, d)) * 0.3
+        y = rng.normal(size=(m, d)) * 0.3 + 0.05
+        gh = -(y ** 2).sum(1) + rng.normal(scale=0.1, size=m)
+        log_b = np.full(m, -np.log(m - 17))
+        y[m - 17:] = 0.0                                    # padded columns, as _Cloud makes them
+        gh[m - 17:] = rng.normal(size=17)
+        log_b[m - 17:] = ref_sk.PAD_LOG_WEIGHT
+        off = rng.normal(scale=0.3, size=k)
+        xsq = (x * x).sum(1)
+        for tag, dt in (("f64", torch.float64), ("f32", torch.float32)):
+            t = lambda a: torch.as_tensor(a, dtype=dt)
+            fh = ref_sk._half_step(t(x), t(xsq), t(off), t(y.T.copy()), t(gh), t(log_b),
+                                   t(1.0 / eps), t(eps), t(kappa))
+            out[f"c{cid}_fh_{tag}"] = fh.numpy().astype(np.float64)
+        out.update({f"c{cid}_x": x, f"c{cid}_y": y, f"c{cid}_gh": gh, f"c{cid}_log_b": log_b, f"c{cid}_off": off,
+                    f"c{cid}_xsq": xsq, f"c{cid}_eps": eps, f"c{cid}_kappa": kappa})
+    out["ncases"] = len(cases)
+    np.savez_compressed(HERE / "half_step_kat.npz", **out)
+
+
+def row_lse_kat():
+    from scipy.special import logsumexp
+    rows, m, d, eps, real = 256, 1024, 64, 0.1, 1024 - 300
+    rng = np.random.default_rng(0)
+    x = rng.normal(size=(rows, d)) * 0.15
+    y = rng.normal(size=(m, d)) * 0.15 + 0.02
+    gh = -(y ** 2).sum(1) + rng.normal(scale=0.05, size=m)
+    log_b = np.full(m, -np.log(m))
+    y[real:] = 0.0
+    gh[real:] = 0.0
+    log_b[real:] = -1e9
+    xa_T = np.vstack([x.T, np.ones((1, rows))]).astype(np.float32)
+    ya_T = np.vstack([2.0 / eps * y.T, (gh / eps + log_b)[None, :]]).astype(np.float32)
+    ref = logsumexp(xa_T.astype(np.float64).T @ ya_T.astype(np.float64), axis=1)
+    np.savez_compressed(HERE / "row_lse_kat.npz", xa_T=xa_T, ya_T=ya_T, lse=ref)
+
+
+def _res(prefix, r, out):
+    out[prefix + "_f"], out[prefix + "_g"] = r.f, r.g
+    out[prefix + "_meta"] = np.array([r.iterations, r.error, float(r.converged), r.cost, r.cost_scale])
+    out[prefix + "_center"] = r.center
+    if r.row_mass is not None:
+        out[prefix + "_row_mass"], out[prefix + "_col_mass"] = r.row_mass, r.col_mass
+
+
+def solver_cases():
+    from trnopt.singlecell import wot_eps_stages
+    SO = ref_sk.SinkhornOptions
+    out = {}
+    x, y = clouds()
+    for tag, be, tol in (("f64", CPU64, 1e-7), ("f32", CPU32, 1e-5)):
+        o = dict(eps=0.1, tol=tol, max_iters=5000, backend=be)
+        _res(f"balanced_{tag}", ref_sk.sinkhorn(x, y, opts=SO(**o)), out)
+        _res(f"blocked_{tag}", ref_sk.sinkhorn(x, y, opts=SO(block=32, block_y=40, **o)), out)
+        a = np.random.default_rng(1).uniform(0.5, 1.5, len(x)) / len(x)
+        _res(f"unbalanced_{tag}", ref_sk.sinkhorn(x, y, a=a, opts=SO(rho=1.0, block=50, **o)), out)
+        rng = np.random.default_rng(2)
+        wa = rng.uniform(0.2, 1.0, len(x)); wa /= wa.sum()
+        wb = rng.uniform(0.2, 1.0, len(y)); wb /= wb.sum()
+        _res(f"weighted_{tag}", ref_sk.sinkhorn(x, y, wa, wb, SO(**o)), out)
+        _res(f"fixed7_{tag}", ref_sk.sinkhorn(x, y, opts=SO(max_iters=7, fixed_iters=True, backend=be)), out)
+        x2, y2 = clouds(n=90, m=70, d=4, seed=7)
+        G = np.random.default_rng(8).uniform(0.5, 2.0, len(x2))
+        I, J = len(x2), len(y2)
+        for staged in (False, True):
+            so = SO(eps=0.2, rho=(1.0, 50.0), normalize="median", tol=tol / 10, max_iters=20_000, check_every=5,
+                    backend=be, eps_stages=wot_eps_stages(0.2) if staged else None)
+            r = ref_sk.sinkhorn(x2, y2, np.full(I, 1 / I), np.full(J, 1 / J), so, a_target=G / I,
+                                b_target=np.full(J, G.mean() / J))
+            _res(f"wot{'_staged' if staged else ''}_{tag}", r, out)
+    x3, y3 = clouds(n=300, m=250, d=10, seed=3)
+    o = dict(eps=0.01, tol=1e-6, max_iters=20_000)
+    _res("epsplain_f64", ref_sk.sinkhorn(x3, y3, opts=SO(**o)), out)
+    _res("epsscaled_f64", ref_sk.sinkhorn(x3, y3, opts=SO(eps_start=2.0, eps_decay=0.8, **o)), out)
+    np.savez_compressed(HERE / "solver_cases.npz", **out)
+
+
+def cfg1():
+    x, y = synthetic.cfg1()
+    out, res = {}, {}
+    for tag, be in (("f64", CPU64), ("f32", CPU32)):
+        res[tag] = r = ref_sk.sinkhorn(x, y, opts=ref_sk.SinkhornOptions(eps=0.1, max_iters=200, fixed_iters=True,
+                                                                         normalize=False, backend=be))
+        out[f"f_{tag}"], out[f"g_{tag}"] = r.f, r.g
+    P = ref_sk.transport_plan(x, y, res["f64"])
+    out["row_sum_f64"], out["col_sum_f64"] = P.sum(1), P.sum(0)
+    np.savez_compressed(HERE / "cfg1.npz", **out)
+
+
+def normalization():
+    out = {}
+    cases = [("a", 137, 91, 5, 0), ("b", 90, 70, 4, 7), ("c", 301, 250, 10, 3), ("d", 1000, 1200, 30, 11)]
+    for tag, n, m, d, seed in cases:
+        x, y = clouds(n, m, d, seed)
+        for how in ("mean", "median"):
+            c, s = ref_sk.normalization(x, y, how=how)
+            out[f"{tag}_{how}_center"], out[f"{tag}_{how}_scale"] = c, s
+    x0, x1, _ = synthetic.cfg3()
+    c, s = ref_sk.normalization(x0, x1, how="median")
+    out["cfg3_median_center"], out["cfg3_median_scale"] = c, s
+    x5, y5 = synthetic.cfg5(n=20_000)
+    c, s = ref_sk.normalization(x5, y5, how="mean")
+    out["cfg5s_mean_center"], out["cfg5s_mean_scale"] = c, s
+    np.savez_compressed(HERE / "normalization.npz", **out)
+
+
+def wot_small():
+    x0, x1, growth = synthetic.cfg3(n=735, m=896)
+    opts = ref_sk.SinkhornOptions(backend=CPU64)
+    tm = wot_transport_map(x0, x1, growth, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8,
+                           opts=opts)
+    r = tm.result
+    np.savez_compressed(HERE / "wot_small.npz", f=r.f, g=r.g, row_mass=r.row_mass, col_mass=r.col_mass,
+                        iterations=tm.iterations, last_iterations=r.iterations, cost_scale=r.cost_scale,
+                        center=r.center, learned=np.stack(tm.learned_growth))
+
+
+if __name__ == "__main__":
+    which = sys.argv[1:] or ["half_step_kat", "row_lse_kat", "solver_cases", "cfg1", "normalization", "wot_small"]
+    for w in which:
+        print("generating", w, flush=True)
+        globals()[w]()

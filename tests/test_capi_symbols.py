@@ -1,0 +1,38 @@
+"""The C-ABI library loads without a GPU and exports every function include/trnopt_cuda.h declares. CPU only: no
+compute call is made here."""
+
+import ctypes
+import re
+
+from conftest import ROOT
+
+
+def declared_functions():
+    text = (ROOT / "include" / "trnopt_cuda.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(trnopt_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_api():
+    names = declared_functions()
+    for must in ("trnopt_half_step", "trnopt_row_lse", "trnopt_workspace_size", "trnopt_median_cost"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from trnopt import _capi
+    lib = ctypes.CDLL(str(_capi.LIB_PATH))
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    from trnopt import _capi
+    assert sorted(_capi.exported_symbols()) == declared_functions()
+
+
+def test_status_strings_without_gpu():
+    from trnopt import _capi
+    assert _capi.lib.trnopt_status_string(0) == b"ok"
+    assert _capi.lib.trnopt_status_string(-3) == b"workspace missing or too small"
+    assert _capi.lib.trnopt_version() >= 100

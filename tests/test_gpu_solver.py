@@ -1,0 +1,138 @@
+"""The whole solver on the GPU (Backend.preset("cuda-fused")) against the reference's answers.
+
+Parity bar: potentials within max|delta f| / eps <= 1e-4 of the reference's float64 CPU
+solver on identical seeded inputs (balanced potentials are compared after removing the gauge constant
+f + c, g - c that leaves the plan unchanged), and the plan's row and column sums within 1e-5 relative L1.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import trnopt_oracle as O
+from trnopt import Backend, SinkhornOptions, sinkhorn, synthetic, transport_plan
+
+pytestmark = pytest.mark.gpu
+BE = Backend.preset("cuda-fused")
+POT_TOL = 1e-4         # max |delta f| / eps
+MARG_TOL = 1e-5        # relative L1 of plan row / column sums
+
+
+def clouds(n=137, m=91, d=5, seed=0):
+    rng = np.random.default_rng(seed)
+    return rng.normal(size=(n, d)), rng.normal(size=(m, d)) * 0.8 + 0.5
+
+
+def gauge_err(f, g, f_ref, g_ref, eps, balanced=True):
+    df, dg = f - f_ref, g - g_ref
+    c = (df.mean() - dg.mean()) / 2 if balanced else 0.0
+    return max(np.abs(df - c).max(), np.abs(dg + c).max()) / eps
+
+
+def rel_l1(a, b):
+    return np.abs(a - b).sum() / np.abs(b).sum()
+
+
+def plan_err(P, Q):
+    return np.abs(P - Q).max() / Q.max()
+
+
+def test_cfg1_matches_reference_float64(golden):
+    """Config 1: 2,000^2, d 16, U[0,1], eps 0.1, 200 fixed iterations, raw cost."""
+    z = golden("cfg1.npz")
+    x, y = synthetic.cfg1()
+    r = sinkhorn(x, y, opts=SinkhornOptions(eps=0.1, max_iters=200, fixed_iters=True, normalize=False, backend=BE))
+    assert r.iterations == 200
+    err = gauge_err(r.f, r.g, z["f_f64"], z["g_f64"], 0.1)
+    rows, cols = O.plan_marginals(x, y, r.f, r.g, 0.1, r.center, r.cost_scale)
+    ref32 = gauge_err(z["f_f32"], z["g_f32"], z["f_f64"], z["g_f64"], 0.1)
+    assert err <= POT_TOL, (err, ref32)
+    assert rel_l1(rows, z["row_sum_f64"]) <= MARG_TOL
+    assert rel_l1(cols, z["col_sum_f64"]) <= MARG_TOL
+
+
+def test_balanced_cases_match_reference(golden):
+    z = golden("solver_cases.npz")
+    x, y = clouds()
+    o = dict(eps=0.1, tol=1e-5, max_iters=5000, backend=BE)
+    r = sinkhorn(x, y, opts=SinkhornOptions(**o))
+    assert r.converged
+    P_ref = transport_plan(x, y, _as_result(z, "balanced_f64", r))
+    assert plan_err(transport_plan(x, y, r), P_ref) < 2e-3
+    P = transport_plan(x, y, r)
+    np.testing.assert_allclose(P.sum(axis=1), 1 / len(x), rtol=2e-2)
+    np.testing.assert_allclose(P.sum(axis=0), 1 / len(y), rtol=2e-2 + 1e-5)
+    blk = sinkhorn(x, y, opts=SinkhornOptions(block=32, block_y=40, **o))
+    assert plan_err(transport_plan(x, y, blk), P) < 2e-3 and abs(blk.cost - r.cost) < 2e-3 * (1 + abs(r.cost))
+    rng = np.random.default_rng(2)
+    wa = rng.uniform(0.2, 1.0, len(x)); wa /= wa.sum()
+    wb = rng.uniform(0.2, 1.0, len(y)); wb /= wb.sum()
+    rw = sinkhorn(x, y, wa, wb, SinkhornOptions(**o))
+    assert plan_err(transport_plan(x, y, rw, wa, wb), transport_plan(x, y, _as_result(z, "weighted_f64", rw), wa, wb)) < 2e-3
+
+
+def _as_result(z, prefix, like):
+    from dataclasses import replace
+    return replace(like, f=z[prefix + "_f"], g=z[prefix + "_g"], center=z[prefix + "_center"],
+                   cost_scale=float(z[prefix + "_meta"][4]))
+
+
+def test_fixed_iters_matches_reference(golden):
+    z = golden("solver_cases.npz")
+    x, y = clouds()
+    r = sinkhorn(x, y, opts=SinkhornOptions(max_iters=7, fixed_iters=True, backend=BE))
+    assert r.iterations == 7 and not r.converged
+    assert gauge_err(r.f, r.g, z["fixed7_f64_f"], z["fixed7_f64_g"], 0.05) <= POT_TOL
+
+
+def test_unbalanced_matches_reference(golden):
+    z = golden("solver_cases.npz")
+    x, y = clouds()
+    a = np.random.default_rng(1).uniform(0.5, 1.5, len(x)) / len(x)
+    r = sinkhorn(x, y, a=a, opts=SinkhornOptions(eps=0.1, rho=1.0, tol=1e-5, max_iters=5000, block=50, backend=BE))
+    assert r.converged
+    np.testing.assert_allclose(r.f, z["unbalanced_f64_f"], atol=1e-4)
+    assert rel_l1(r.row_mass, z["unbalanced_f64_row_mass"]) <= 1e-4
+
+
+@pytest.mark.parametrize("staged", [False, True])
+def test_wot_formulation_matches_reference(golden, staged):
+    from trnopt.singlecell import wot_eps_stages
+    z = golden("solver_cases.npz")
+    x, y = clouds(n=90, m=70, d=4, seed=7)
+    G = np.random.default_rng(8).uniform(0.5, 2.0, len(x))
+    I, J = len(x), len(y)
+    o = SinkhornOptions(eps=0.2, rho=(1.0, 50.0), normalize="median", tol=1e-6, max_iters=20_000, check_every=5,
+                        backend=BE, eps_stages=wot_eps_stages(0.2) if staged else None)
+    r = sinkhorn(x, y, np.full(I, 1 / I), np.full(J, 1 / J), o, a_target=G / I, b_target=np.full(J, G.mean() / J))
+    assert r.converged
+    p = f"wot{'_staged' if staged else ''}_f64"
+    assert rel_l1(r.row_mass, z[p + "_row_mass"]) <= 1e-4
+    assert rel_l1(r.col_mass, z[p + "_col_mass"]) <= 1e-4
+
+
+def test_wot_transport_map_reduced_cfg3(golden):
+    """Config 3's settings (median cost, eps 0.05, lambda (1, 50), 3 growth iterations, tol 1e-8 -> 5e-6 in
+    float32) on a reduced pair, against the reference's float64 run."""
+    from trnopt.singlecell import wot_transport_map
+    z = golden("wot_small.npz")
+    x0, x1, growth = synthetic.cfg3(n=735, m=896)
+    tm = wot_transport_map(x0, x1, growth, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8,
+                           opts=SinkhornOptions(backend=BE))
+    r = tm.result
+    assert abs(r.cost_scale - float(z["cost_scale"])) <= 1e-14 * r.cost_scale
+    assert gauge_err(r.f, r.g, z["f"], z["g"], 0.05, balanced=False) <= 10 * POT_TOL
+    assert rel_l1(r.row_mass, z["row_mass"]) <= 1e-4
+    assert rel_l1(r.col_mass, z["col_mass"]) <= 1e-4
+
+
+def test_cfg2_full_size_column_sums():
+    """Config 2 at full size (10k^2, d 64): after the g half-step the plan's columns sum to b. Checked in float64
+    on the host for 48 random columns (size-independent property)."""
+    x, y = synthetic.cfg2()
+    r = sinkhorn(x, y, opts=SinkhornOptions(eps=0.1, max_iters=20, fixed_iters=True, normalize=False, backend=BE))
+    cols = np.random.default_rng(0).choice(len(y), 48, replace=False)
+    C = (x * x).sum(1)[:, None] + (y[cols] * y[cols]).sum(1)[None, :] - 2.0 * (x @ y[cols].T)
+    logP = -np.log(len(x)) - np.log(len(y)) + (r.f[:, None] + r.g[None, cols] - C) / 0.1
+    mx = logP.max(0)
+    col_sum = np.exp(mx) * np.exp(logP - mx).sum(0)
+    np.testing.assert_allclose(col_sum * len(y), 1.0, rtol=1e-4)

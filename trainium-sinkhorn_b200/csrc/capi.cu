@@ -1,0 +1,182 @@
+// C ABI of libtrnopt_cuda.so: argument checks, workspace layout and dispatch to the kernels.
+// The declarations, with the reference interface each entry point replaces, are in include/trnopt_cuda.h.
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/trnopt_cuda.h"
+#include "kernels.h"
+
+namespace trnopt {
+
+__device__ int g_error_word;
+int* device_error_word() {
+  int* p = nullptr;
+  cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word);
+  return p;
+}
+
+}  // namespace trnopt
+
+using namespace trnopt;
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return TRNOPT_OK;
+  t_last_cuda_error = (int)e;
+  return TRNOPT_ERR_CUDA;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr size_t kCounterRegion = 256;   // bytes reserved per 64 row tiles for the arrival counters
+
+size_t counter_bytes(int nrt) { return ((size_t)nrt * sizeof(int) + kCounterRegion - 1) / kCounterRegion * kCounterRegion; }
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+// Carve the workspace: [counters (nrt ints, 256-byte padded)][partials].
+int bind_workspace(StreamK& sk, size_t partial_bytes, void* ws, size_t ws_bytes) {
+  const size_t need = counter_bytes(sk.nrt) + partial_bytes;
+  if (ws == nullptr || ws_bytes < need) return TRNOPT_ERR_WORKSPACE;
+  if (!aligned(ws, 256)) return TRNOPT_ERR_ALIGNMENT;
+  sk.counters = reinterpret_cast<int*>(ws);
+  sk.partials = reinterpret_cast<float2*>(reinterpret_cast<char*>(ws) + counter_bytes(sk.nrt));
+  return TRNOPT_OK;
+}
+
+int check_points(const float* pT, int ld, int count, int d) {
+  if (pT == nullptr || count < 1 || d < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (ld < count) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (ld % 4 != 0 || !aligned(pT, 16)) return TRNOPT_ERR_ALIGNMENT;
+  return TRNOPT_OK;
+}
+
+int ffma_run(LseProblem& p, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  StreamK sk{};
+  ffma_plan(current_device(), p.rows, p.m, p.d, sk);
+  int st = bind_workspace(sk, ffma_partial_bytes(sk), ws, ws_bytes);
+  if (st != TRNOPT_OK) return st;
+  p.error_word = device_error_word();
+  return cuda_status(ffma_launch(p, sk, stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int trnopt_version(void) { return 100; }
+
+const char* trnopt_status_string(int status) {
+  switch (status) {
+    case TRNOPT_OK: return "ok";
+    case TRNOPT_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TRNOPT_ERR_ALIGNMENT: return "misaligned pointer or leading dimension";
+    case TRNOPT_ERR_WORKSPACE: return "workspace missing or too small";
+    case TRNOPT_ERR_UNSUPPORTED: return "unsupported shape or path";
+    case TRNOPT_ERR_CUDA: return "CUDA runtime error";
+    case TRNOPT_ERR_DEVICE: return "a kernel reported an error flag";
+    default: return "unknown status";
+  }
+}
+
+int trnopt_last_cuda_error(void) { return t_last_cuda_error; }
+
+int trnopt_device_error_flags(void* stream, int* flags_out) {
+  if (flags_out == nullptr) return TRNOPT_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int flags = 0;
+  int st = cuda_status(cudaMemcpyFromSymbolAsync(&flags, g_error_word, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
+  if (st == TRNOPT_OK) st = cuda_status(cudaStreamSynchronize(s));
+  if (st != TRNOPT_OK) return st;
+  if (flags != 0) {
+    const int zero = 0;
+    st = cuda_status(cudaMemcpyToSymbolAsync(g_error_word, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
+    if (st == TRNOPT_OK) st = cuda_status(cudaStreamSynchronize(s));
+  }
+  *flags_out = flags;
+  return st;
+}
+
+size_t trnopt_workspace_size(int rows, int m, int d, int path) {
+  if (rows < 1 || m < 1 || d < 1) return 0;
+  StreamK sk{};
+  size_t partial = 0;
+  if (path == TRNOPT_PATH_FFMA) {
+    ffma_plan(current_device(), rows, m, d, sk);
+    partial = ffma_partial_bytes(sk);
+  } else {
+    return 0;
+  }
+  return counter_bytes(sk.nrt) + partial;
+}
+
+int trnopt_workspace_init(void* workspace, size_t ws_bytes, void* stream) {
+  if (workspace == nullptr || ws_bytes == 0) return TRNOPT_ERR_INVALID_ARGUMENT;
+  return cuda_status(cudaMemsetAsync(workspace, 0, ws_bytes, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_half_step(const float* xT, int ldx, const float* xsq, const float* off, const float* yT, int ldy,
+                     const float* gh, const float* log_b, int rows, int m, int d, float eps, float kappa, float* fh,
+                     void* workspace, size_t ws_bytes, void* stream) {
+  if (d > 128) return TRNOPT_ERR_UNSUPPORTED;
+  int st = check_points(xT, ldx, rows, d);
+  if (st == TRNOPT_OK) st = check_points(yT, ldy, m, d);
+  if (st != TRNOPT_OK) return st;
+  if (xsq == nullptr || gh == nullptr || log_b == nullptr || fh == nullptr) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  LseProblem p{};
+  p.xT = xT; p.ldx = ldx; p.yT = yT; p.ldy = ldy; p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off;
+  p.rows = rows; p.m = m; p.d = d;
+  const double inv_eps = 1.0 / (double)eps;
+  p.dot2 = (float)(2.0 * inv_eps * 1.4426950408889634);
+  p.gh2 = (float)(inv_eps * 1.4426950408889634);
+  p.lb2 = kLog2e;
+  p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
+  return ffma_run(p, workspace, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int trnopt_row_lse(const float* xaT, int ldx, const float* yaT, int ldy, int rows, int m, int k, float* lse,
+                   void* workspace, size_t ws_bytes, void* stream) {
+  if (k > 128) return TRNOPT_ERR_UNSUPPORTED;
+  int st = check_points(xaT, ldx, rows, k);
+  if (st == TRNOPT_OK) st = check_points(yaT, ldy, m, k);
+  if (st != TRNOPT_OK) return st;
+  if (lse == nullptr) return TRNOPT_ERR_INVALID_ARGUMENT;
+  LseProblem p{};
+  p.xT = xaT; p.ldx = ldx; p.yT = yaT; p.ldy = ldy; p.rows = rows; p.m = m; p.d = k;
+  p.dot2 = kLog2e; p.gh2 = 0.f; p.lb2 = 0.f; p.eps = 1.0; p.kappa = 1.0; p.mode = 1; p.out = lse;
+  return ffma_run(p, workspace, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t trnopt_median_workspace_size(void) { return median_workspace_bytes(); }
+
+int trnopt_median_cost(const double* xc, const double* yc, const double* sqx, const double* sqy, int n, int m, int d,
+                       double* out, void* workspace, size_t ws_bytes, void* stream) {
+  if (!xc || !yc || !sqx || !sqy || !out || n < 1 || m < 1 || d < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (d > 128) return TRNOPT_ERR_UNSUPPORTED;
+  if ((long long)n * (long long)m > 100000000ll) return TRNOPT_ERR_UNSUPPORTED;
+  if (workspace == nullptr || ws_bytes < median_workspace_bytes()) return TRNOPT_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(xc, 8) || !aligned(yc, 8)) return TRNOPT_ERR_ALIGNMENT;
+  return cuda_status(median_launch(xc, yc, sqx, sqy, n, m, d, out, workspace, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float* w, int n, float inv_eps,
+                          float* out, void* stream) {
+  if (!gh_old || !gh_new || !w || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  return cuda_status(balanced_error_launch(gh_old, gh_new, w, n, inv_eps, out, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream) {
+  if (!gh_old || !gh_new || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  return cuda_status(max_change_launch(gh_old, gh_new, n, inv_eps, out, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

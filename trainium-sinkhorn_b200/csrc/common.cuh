@@ -1,0 +1,124 @@
+// Shared device/host pieces of the fused Sinkhorn half-step kernels (sm_100a).
+//
+// The half-step of trnopt (reference src/trnopt/sinkhorn.py:108-119) computes, for every row i of one cloud,
+//     lse_i = log sum_j exp( z_ij ),   z_ij = (2 x_i . y_j + gh_j) / eps + log b_j
+//     fh_i  = kappa * (|x_i|^2 + eps * off_i - eps * lse_i) - |x_i|^2
+// The kernels here keep z in registers (never in memory) in base-2 units, t_ij = z_ij * log2(e), and carry an
+// online (max M, sum l) pair per row, sum l = sum_j 2^(t_ij - M).
+//
+// Work split ("stream-K"): the (row tile, column tile) grid is linearised row-major into U units and CTA k of G
+// takes units [k U / G, (k+1) U / G). A CTA's run inside one row tile is a segment; every segment ends with a
+// partial (M, l) per row written to the workspace and one arrival on the row tile's counter. The arrival that
+// completes a row tile merges its partials and writes the output rows, then resets the counter to zero, so the
+// workspace is left ready for the next launch on the same stream.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace trnopt {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr double kLn2 = 0.6931471805599453;
+// Running-max floor: below every real score (padding scores are about -1.4e9 in base-2 units) and finite, so
+// 2^(t - M) never sees inf - inf. Columns past m get bias -inf and contribute exactly 0.
+constexpr float kMaxFloor = -1.0e30f;
+
+// Device error word: bit flags set by kernels that give up a bounded wait. Read and cleared by the host API.
+enum ErrorBits : int {
+  kErrWaitTimeout = 1,   // an mbarrier / pipeline wait ran out of its time limit
+  kErrTmemAlloc = 2,     // tensor-memory allocation did not return in time
+  kErrBadLaunch = 4,     // a launch-shape invariant did not hold on the device
+};
+
+struct LseProblem {
+  const float* xT;     // row side points, transposed: xT[k * ldx + i], k < d, i < rows
+  int ldx;
+  const float* yT;     // column side points, transposed: yT[k * ldy + j], j < m
+  int ldy;
+  const float* gh;     // (m,) shifted potential of the column side; nullptr = 0
+  const float* log_b;  // (m,) log weights of the column side; nullptr = 0
+  const float* xsq;    // (rows,) |x_i|^2 (fh mode only)
+  const float* off;    // (rows,) log(target / reference) of the rows; nullptr = 0 (fh mode only)
+  int rows, m, d;
+  float dot2;          // multiplier of x.y in base-2 units: 2 log2(e) / eps (fh) or log2(e) (lse)
+  float gh2;           // multiplier of gh: log2(e) / eps
+  float lb2;           // multiplier of log b: log2(e)
+  double eps, kappa;   // fh epilogue
+  int mode;            // 0: write fh, 1: write lse (natural log)
+  float* out;          // (rows,)
+  int* error_word;     // device error flags
+};
+
+// Stream-K bookkeeping, computed on the host per launch.
+struct StreamK {
+  int nrt, nct;        // row tiles, column tiles
+  long long units;     // nrt * nct
+  int grid;            // G, <= units
+  int slots;           // partial slots per row tile and per producer (>= the most CTAs touching a row tile)
+  int parts_per_cta;   // partials one CTA writes per segment (1 for the FFMA kernel, 2 for the tcgen05 kernel)
+  int* counters;       // (nrt,) arrival counters, zero between launches
+  float2* partials;    // (nrt, slots * parts_per_cta, BM) of (M, l)
+};
+
+__host__ __device__ inline long long sk_unit_begin(long long k, long long units, long long grid) {
+  return (k * units) / grid;
+}
+
+// The CTA whose range holds unit u: the largest k with floor(k U / G) <= u, i.e. ceil((u + 1) G / U) - 1.
+__host__ __device__ inline int sk_cta_of(long long u, long long units, long long grid) {
+  return (int)(((u + 1) * grid + units - 1) / units - 1);
+}
+
+// Host: size the partial buffer. A row tile of nct units can be touched by at most ceil(nct G / U) + 1 CTAs.
+inline int sk_max_slots(long long units, long long grid, int nct) {
+  long long s = (nct * grid + units - 1) / units + 1;
+  return (int)s;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Merge of two online (max, sum) pairs in base 2.
+__device__ __forceinline__ void lse_merge(float& M, float& l, float M2, float l2) {
+  float Mn = fmaxf(M, M2);
+  l = l * ex2_approx(M - Mn) + l2 * ex2_approx(M2 - Mn);
+  M = Mn;
+}
+
+// Finish one row: merge nparts partials (M, l) in double precision and apply the kappa / off epilogue
+// (reference src/trnopt/sinkhorn.py:119, src/trnopt/nki_sinkhorn.py:212-225).
+__device__ inline void finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride) {
+  float M = kMaxFloor;
+  for (int s = 0; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
+  double l = 0.0;
+  for (int s = 0; s < nparts; ++s) {
+    float2 v = __ldcg(&parts[(size_t)s * stride]);
+    if (v.y > 0.f) l += (double)v.y * exp2((double)v.x - (double)M);
+  }
+  double lse = ((double)M + log2(l)) * kLn2;
+  double res;
+  if (p.mode == 0) {
+    double xsq = (double)p.xsq[row];
+    double off = p.off ? (double)p.off[row] : 0.0;
+    res = p.kappa * (xsq + p.eps * off - p.eps * lse) - xsq;
+  } else {
+    res = lse;
+  }
+  p.out[row] = (float)res;
+}
+
+// Bounded-wait helpers ---------------------------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr unsigned long long kWaitLimitNs = 4000000000ull;   // 4 s: no legitimate wait in these kernels is close
+
+}  // namespace trnopt

@@ -1,0 +1,151 @@
+"""ctypes binding of libtrnopt_cuda.so (the C ABI declared in include/trnopt_cuda.h).
+
+There is no fallback: if the library is missing, importing this module raises ImportError telling how to build it,
+and every wrapper raises TrnoptError when the C call returns a negative status. Tensors are passed as raw device
+pointers with the current torch CUDA stream, so calls queue asynchronously like any other kernel on that stream.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(os.environ.get("TRNOPT_CUDA_LIB", Path(__file__).resolve().parent / "libtrnopt_cuda.so"))
+
+PATH_FFMA, PATH_TC = 0, 1
+
+
+class TrnoptError(RuntimeError):
+    """A negative status from the C ABI (argument, alignment, workspace, CUDA or device-flag error)."""
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is not built: run `python trainium-sinkhorn_b200/trnopt/_build.py` "
+                          "(or __graft_entry__.build()); this package has no CPU fallback")
+    return ctypes.CDLL(str(LIB_PATH))
+
+
+lib = _load()
+
+_P, _I, _F, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+_SIGS = {
+    "trnopt_version": (_I, []),
+    "trnopt_status_string": (ctypes.c_char_p, [_I]),
+    "trnopt_last_cuda_error": (_I, []),
+    "trnopt_device_error_flags": (_I, [_P, ctypes.POINTER(_I)]),
+    "trnopt_workspace_size": (_Z, [_I, _I, _I, _I]),
+    "trnopt_workspace_init": (_I, [_P, _Z, _P]),
+    "trnopt_half_step": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _I, _I, _I, _F, _F, _P, _P, _Z, _P]),
+    "trnopt_row_lse": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _P, _Z, _P]),
+    "trnopt_balanced_error": (_I, [_P, _P, _P, _I, _F, _P, _P]),
+    "trnopt_max_change": (_I, [_P, _P, _I, _F, _P, _P]),
+    "trnopt_median_workspace_size": (_Z, []),
+    "trnopt_median_cost": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
+}
+for _name, (_res, _args) in _SIGS.items():
+    _fn = getattr(lib, _name)
+    _fn.restype, _fn.argtypes = _res, _args
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = lib.trnopt_status_string(status).decode()
+        extra = f" (cudaError {lib.trnopt_last_cuda_error()})" if status == -5 else ""
+        raise TrnoptError(f"{what}: {msg}{extra}")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t: torch.Tensor, name: str, dtype=torch.float32) -> None:
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous {dtype} CUDA tensor")
+
+
+def workspace_size(rows: int, m: int, d: int, path: int = PATH_FFMA) -> int:
+    return int(lib.trnopt_workspace_size(rows, m, d, path))
+
+
+def new_workspace(nbytes: int, device) -> torch.Tensor:
+    """A zeroed workspace from the torch caching allocator (256-byte aligned)."""
+    ws = torch.empty(max(256, nbytes), dtype=torch.uint8, device=device)
+    check(lib.trnopt_workspace_init(_ptr(ws), ws.numel(), _stream()), "trnopt_workspace_init")
+    return ws
+
+
+def half_step(xT, ldx, xsq, off, yT, ldy, gh, log_b, rows, m, d, eps, kappa, fh, ws) -> None:
+    """Queue the FFMA fused half-step: fh[:rows] from the transposed clouds xT (d, ldx) and yT (d, ldy)."""
+    check(lib.trnopt_half_step(_ptr(xT), ldx, _ptr(xsq), _ptr(off), _ptr(yT), ldy, _ptr(gh), _ptr(log_b), rows, m,
+                               d, float(eps), float(kappa), _ptr(fh), _ptr(ws), ws.numel(), _stream()),
+          "trnopt_half_step")
+
+
+def row_lse(xaT: torch.Tensor, yaT: torch.Tensor, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """lse_i = log sum_j exp(xa_i . ya_j) for xa_T (k, rows), ya_T (k, m) (the reference's row-LSE kernel)."""
+    _need(xaT, "xa_T")
+    _need(yaT, "ya_T")
+    k, rows = xaT.shape
+    m = yaT.shape[1]
+    if yaT.shape[0] != k:
+        raise ValueError("xa_T and ya_T need the same number of rows (contraction length)")
+    xaT, ldx = _pad_ld(xaT)
+    yaT, ldy = _pad_ld(yaT)
+    if ws is None:
+        ws = new_workspace(workspace_size(rows, m, k, PATH_FFMA), xaT.device)
+    out = torch.empty(rows, dtype=torch.float32, device=xaT.device)
+    check(lib.trnopt_row_lse(_ptr(xaT), ldx, _ptr(yaT), ldy, rows, m, k, _ptr(out), _ptr(ws), ws.numel(),
+                             _stream()), "trnopt_row_lse")
+    return out
+
+
+def _pad_ld(t: torch.Tensor):
+    """Copy a (k, n) matrix into one whose leading dimension is a multiple of 4 (the 16-byte row rule)."""
+    k, n = t.shape
+    ld = -(-n // 4) * 4
+    if ld == n and t.data_ptr() % 16 == 0:
+        return t, ld
+    out = torch.zeros((k, ld), dtype=t.dtype, device=t.device)
+    out[:, :n] = t
+    return out, ld
+
+
+def balanced_error(gh_old, gh_new, w, n, inv_eps, out) -> None:
+    check(lib.trnopt_balanced_error(_ptr(gh_old), _ptr(gh_new), _ptr(w), n, float(inv_eps), _ptr(out), _stream()),
+          "trnopt_balanced_error")
+
+
+def max_change(gh_old, gh_new, n, inv_eps, out) -> None:
+    check(lib.trnopt_max_change(_ptr(gh_old), _ptr(gh_new), n, float(inv_eps), _ptr(out), _stream()),
+          "trnopt_max_change")
+
+
+def median_cost(xc: torch.Tensor, yc: torch.Tensor, sqx: torch.Tensor, sqy: torch.Tensor) -> torch.Tensor:
+    """Exact median of all clamped costs (float64 device scalar in a 1-element tensor)."""
+    for t, nm in ((xc, "xc"), (yc, "yc"), (sqx, "sqx"), (sqy, "sqy")):
+        _need(t, nm, torch.float64)
+    n, d = xc.shape
+    m = yc.shape[0]
+    ws = torch.empty(int(lib.trnopt_median_workspace_size()), dtype=torch.uint8, device=xc.device)
+    out = torch.empty(1, dtype=torch.float64, device=xc.device)
+    check(lib.trnopt_median_cost(_ptr(xc), _ptr(yc), _ptr(sqx), _ptr(sqy), n, m, d, _ptr(out), _ptr(ws), ws.numel(),
+                                 _stream()), "trnopt_median_cost")
+    return out
+
+
+def device_error_flags() -> int:
+    flags = ctypes.c_int(0)
+    check(lib.trnopt_device_error_flags(_stream(), ctypes.byref(flags)), "trnopt_device_error_flags")
+    return int(flags.value)

@@ -1,0 +1,343 @@
+"""Entropic optimal transport (log-domain Sinkhorn) with the half-step fused into sm_100a CUDA kernels.
+
+Same API and loop semantics as the reference's src/trnopt/sinkhorn.py (SinkhornOptions, SinkhornResult, sinkhorn,
+transport_plan, normalization); the half-step under the loop is this package's C-ABI library instead of the
+PyTorch _half_step (sinkhorn.py:108-119) or the NKI kernel (nki_sinkhorn.py:175-228):
+
+    f_i = -eps * LSE_j( log b_j + (g_j - C_ij) / eps )      C_ij = |x_i - y_j|^2
+        = |x_i|^2 - eps * LSE_j( log b_j + (gh_j + 2 x_i . y_j) / eps ),   gh = g - |y|^2
+
+computed per row in registers (scores never stored), for all rows of one cloud per launch.
+
+Numerics. The kernels work in float32, like the reference's Trainium and GPU paths. Coordinates are translated so
+that the two clouds' joint mean is the origin before they reach the device (C is unchanged by a translation, and
+the shifted potentials are re-based so the iteration starts from exactly the reference's g = |y|^2 of its own
+frame); this keeps |x|^2 and x.y small and is what the reference's own normalization does when it is on
+(sinkhorn.py:224-225). The returned f, g, center and cost_scale are the reference's.
+
+Multi-GPU. With opts.cores = P > 1 the call must be made on every rank of an initialised torch.distributed
+process group of P ranks (one GPU each, same inputs): each rank computes 1/P of the rows of every half-step and the
+new potential is all-gathered over NCCL, as the reference splits rows across NeuronCores and exchanges the halves
+(sinkhorn.py:295-311).
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _capi
+from .backend import Backend
+
+PAD_LOG_WEIGHT = -1e9          # log weight of a padding point (sinkhorn.py:59)
+_DELTA_CAP = 50.0              # cap on (g_old - g_new) / eps in the balanced marginal check (sinkhorn.py:60)
+ROW_TILE = 128                 # rows per kernel tile: clouds are padded to a multiple of ROW_TILE * shards
+
+
+@dataclass
+class SinkhornOptions:
+    eps: float = 0.05
+    rho: float | tuple | None = None
+    max_iters: int = 2000
+    tol: float = 1e-4
+    check_every: int = 10
+    block: int | None = None       # accepted for compatibility: the fused kernel streams tiles, memory is O(n + m)
+    block_y: int | None = None
+    eps_start: float | None = None
+    eps_decay: float = 0.9
+    eps_stages: tuple | None = None
+    stage_tol: float = 1e-6
+    stage_max_iters: int = 1000
+    normalize: bool | str | tuple = True
+    fixed_iters: bool = False
+    cores: int = 1                 # GPUs (torch.distributed ranks) that split each half-step's rows
+    kernel: str = "auto"           # "auto" / "cuda": the fused CUDA half-step (the only one in this package)
+    backend: Backend = Backend.preset("cuda-fused")
+    cuda_path: str = "ffma"        # "ffma": FP32 FFMA tile kernel
+
+
+@dataclass
+class SinkhornResult:
+    f: np.ndarray
+    g: np.ndarray
+    iterations: int
+    error: float
+    converged: bool
+    cost: float
+    seconds: float
+    eps: float
+    rho: float | tuple | None
+    center: np.ndarray
+    cost_scale: float
+    row_mass: np.ndarray | None = None
+    col_mass: np.ndarray | None = None
+
+
+def _use_cuda(opts: SinkhornOptions, d: int) -> None:
+    """Kernel selection, the counterpart of the reference's _use_nki (sinkhorn.py:196-208): this package has one
+    half-step, so anything but a CUDA float32 backend with kernel "auto" / "cuda" is an error."""
+    if opts.kernel not in ("auto", "cuda"):
+        raise ValueError(f"kernel={opts.kernel!r}: this package runs only the fused CUDA half-step "
+                         "(kernel='cuda' or 'auto')")
+    if not opts.backend.is_cuda_fused:
+        raise ValueError("the fused CUDA half-step needs a CUDA device and float32: "
+                         "use Backend.preset('cuda-fused')")
+    if d > 128:
+        raise ValueError("the fused CUDA half-step supports d <= 128")
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device: the fused CUDA half-step has no CPU fallback")
+
+
+def _log_weights(w, n: int, name: str) -> np.ndarray:
+    """sinkhorn.py:211-217."""
+    if w is None:
+        return np.full(n, -np.log(n))
+    w = np.asarray(w, dtype=np.float64)
+    if w.shape != (n,) or np.any(w <= 0):
+        raise ValueError(f"{name} must be {n} positive weights")
+    return np.log(w)
+
+
+def normalization(x: np.ndarray, y: np.ndarray, samples: int = 20_000, seed: int = 0,
+                  how: str = "mean") -> tuple[np.ndarray, float]:
+    """(center, cost_scale) as the reference's normalization (sinkhorn.py:220-238): the mean of all points, and the
+    mean of `samples` sampled pair costs (how="mean"), or the exact median of all n m clamped costs when
+    n m <= 1e8 (how="median", computed on the GPU by a radix select over costs evaluated on the fly in float64;
+    larger problems use the median of the sampled pairs). The sampled statistics are computed on the host from
+    the same default_rng(seed) draws as the reference."""
+    x = np.asarray(x, dtype=np.float64)
+    y = np.asarray(y, dtype=np.float64)
+    center = np.concatenate([x, y]).mean(axis=0)
+    if how == "median" and len(x) * len(y) <= 100_000_000:
+        from ._median import exact_median_cost
+        scale = exact_median_cost(x - center, y - center)
+        return center, (scale if scale > 0 else 1.0)
+    rng = np.random.default_rng(seed)
+    i, j = rng.integers(len(x), size=samples), rng.integers(len(y), size=samples)
+    dd = ((x[i] - y[j]) ** 2).sum(axis=1)
+    scale = float(np.median(dd) if how == "median" else dd.mean())
+    return center, (scale if scale > 0 else 1.0)
+
+
+class _Cloud:
+    """One point cloud on this rank's GPU, padded to a whole number of row tiles per shard.
+
+    xT (d, npad) float32 transposed points (the layout of the reference's NKI path, sinkhorn.py:159-165), sq the
+    squared norms (float64 on the host, then cast, as sinkhorn.py:149), log_w with PAD_LOG_WEIGHT on padding, w the
+    weights (padding exactly 0), off the row offsets log(target / reference) (0 on padding)."""
+
+    def __init__(self, pts: np.ndarray, log_w: np.ndarray, shards: int, dev: torch.device, off=None):
+        n, d = pts.shape
+        unit = ROW_TILE * shards
+        npad = -(-n // unit) * unit
+        P = np.zeros((npad, d))
+        P[:n] = pts
+        L = np.full(npad, PAD_LOG_WEIGHT)
+        L[:n] = log_w
+        O = np.zeros(npad)
+        if off is not None:
+            O[:n] = off
+        f32 = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32).to(dev)
+        self.n, self.npad, self.d, self.shards = n, npad, d, shards
+        self.xT = f32(P.T)
+        self.sq64 = (P * P).sum(axis=1)
+        self.sq = f32(self.sq64)
+        self.log_w = f32(L)
+        self.w = f32(np.exp(L))
+        self.off = f32(O)
+        self.zero = torch.zeros(npad, dtype=torch.float32, device=dev)
+        self.h2d_bytes = 4 * (P.size + 4 * npad)
+
+
+class _CudaStep:
+    """A half-step with the fused kernel: this rank's share of the rows of `side` against all of `other`, then
+    (P > 1) an all-gather so every rank holds the whole new shifted potential. The counterpart of the reference's
+    _NkiStep (sinkhorn.py:177-193)."""
+
+    def __init__(self, dev: torch.device, shards: int, rank: int, ws: torch.Tensor, group=None):
+        self.dev, self.shards, self.rank, self.ws, self.group = dev, shards, rank, ws, group
+
+    def rows(self, side: _Cloud) -> tuple[int, int]:
+        return _shard_range(side.npad, self.shards, self.rank)
+
+    def __call__(self, side: _Cloud, other: _Cloud, other_h: torch.Tensor, eps: float, kappa: float,
+                 use_off: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+        out = torch.empty(side.npad, dtype=torch.float32, device=self.dev) if out is None else out
+        r0, r1 = self.rows(side)
+        off = side.off if use_off else side.zero
+        _capi.half_step(_Off(side.xT, r0), side.npad, _Off(side.sq, r0), _Off(off, r0), other.xT, other.npad,
+                        other_h, other.log_w, r1 - r0, other.npad, side.d, eps, kappa, _Off(out, r0), self.ws)
+        if self.shards > 1:
+            _gather_rows(out, r0, r1, self.group)
+        return out
+
+
+def _shard_range(npad: int, shards: int, rank: int) -> tuple[int, int]:
+    """Rows [r0, r1) of a padded cloud that `rank` computes: equal contiguous shards of whole row tiles."""
+    if npad % (ROW_TILE * shards):
+        raise ValueError(f"padded size {npad} is not a multiple of {ROW_TILE} * {shards}")
+    per = npad // shards
+    return rank * per, (rank + 1) * per
+
+
+def _gather_rows(out: torch.Tensor, r0: int, r1: int, group=None) -> None:
+    """In-place all-gather of every rank's rows [r0, r1) of `out` into all of `out` (NCCL on GPUs)."""
+    import torch.distributed as dist
+    dist.all_gather_into_tensor(out, out[r0:r1], group=group)
+
+
+class _Off:
+    """A device pointer into a float32 tensor at an element offset (for the ctypes calls)."""
+
+    def __init__(self, t: torch.Tensor, offset: int):
+        self.t, self.offset = t, offset
+
+    def data_ptr(self) -> int:
+        return self.t.data_ptr() + 4 * self.offset
+
+
+def _workspace(X: _Cloud, Y: _Cloud, shards: int, dev: torch.device) -> torch.Tensor:
+    need = max(_capi.workspace_size(X.npad // shards, Y.npad, X.d, _capi.PATH_FFMA),
+               _capi.workspace_size(Y.npad // shards, X.npad, X.d, _capi.PATH_FFMA))
+    return _capi.new_workspace(need, dev)
+
+
+def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target=None,
+             b_target=None) -> SinkhornResult:
+    """Entropic OT between point clouds x (n, d) and y (m, d) with weights a, b (default uniform): the reference's
+    sinkhorn() (sinkhorn.py:241-394) with the half-steps on the GPU.
+
+    a, b are the reference measure of the entropy term, eps KL(P | a b^T). Unbalanced (rho given), the penalties
+    rho KL(P 1 | a_target) and rho KL(P^T 1 | b_target) pull the plan's marginals toward a_target and b_target
+    (default a and b)."""
+    opts = opts or SinkhornOptions()
+    x = np.asarray(x, dtype=np.float64)
+    y = np.asarray(y, dtype=np.float64)
+    log_a, log_b = _log_weights(a, len(x), "a"), _log_weights(b, len(y), "b")
+    balanced = opts.rho is None
+    if balanced and abs(np.exp(log_a).sum() - np.exp(log_b).sum()) > 1e-9 * np.exp(log_a).sum():
+        raise ValueError("balanced OT needs sum(a) == sum(b); pass rho for unbalanced")
+    if balanced and (a_target is not None or b_target is not None):
+        raise ValueError("a_target / b_target are for unbalanced OT (pass rho)")
+    if balanced:
+        rho_x = rho_y = None
+    elif isinstance(opts.rho, (tuple, list)):
+        rho_x, rho_y = opts.rho
+    else:
+        rho_x = rho_y = opts.rho
+    off_x = None if a_target is None else _log_weights(a_target, len(x), "a_target") - log_a
+    off_y = None if b_target is None else _log_weights(b_target, len(y), "b_target") - log_b
+    _use_cuda(opts, x.shape[1])
+    shards = max(1, int(opts.cores))
+    rank, group = 0, None
+    if shards > 1:
+        import torch.distributed as dist
+        if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() != shards:
+            raise ValueError(f"cores={shards} needs an initialised torch.distributed group of {shards} ranks "
+                             "(one GPU per rank, launched with torchrun)")
+        rank = dist.get_rank()
+    dev = opts.backend.torch_device()
+
+    if isinstance(opts.normalize, tuple):
+        center, scale = np.asarray(opts.normalize[0], dtype=np.float64), float(opts.normalize[1])
+    elif opts.normalize:
+        with torch.cuda.device(dev):
+            center, scale = normalization(x, y, how=opts.normalize if isinstance(opts.normalize, str) else "mean")
+    else:
+        center, scale = np.zeros(x.shape[1]), 1.0
+    xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
+    shift = np.concatenate([xs, ys]).mean(axis=0)          # internal frame: joint mean at the origin
+    xi, yi = xs - shift, ys - shift
+
+    with torch.cuda.device(dev):
+        X = _Cloud(xi, log_a, shards, dev, off_x)
+        Y = _Cloud(yi, log_b, shards, dev, off_y)
+        ws = _workspace(X, Y, shards, dev)
+        step = _CudaStep(dev, shards, rank, ws, group)
+
+        sched = []
+        stages = [e for e in (opts.eps_stages or ()) if e > opts.eps]
+        if not stages and opts.eps_start is not None and opts.eps_start > opts.eps:
+            e = opts.eps_start
+            while e > opts.eps and len(sched) < opts.max_iters:
+                sched.append(e)
+                e *= opts.eps_decay
+
+        def kap(e, rho):
+            return 1.0 if rho is None else rho / (rho + e)
+
+        # The reference starts from gh = 0 in its frame, i.e. g = |ys|^2; in the internal frame that is
+        # gh = |ys|^2 - |yi|^2 (exactly the same iteration).
+        gh0 = np.zeros(Y.npad)
+        gh0[:Y.n] = (ys * ys).sum(1) - (yi * yi).sum(1)
+        gh = torch.as_tensor(gh0, dtype=torch.float32).to(dev)
+        fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
+        bufs = [torch.empty(Y.npad, dtype=torch.float32, device=dev) for _ in range(2)]
+        err_dev = torch.zeros(1, dtype=torch.float32, device=dev)
+        err, converged, it = float("nan"), False, 0
+        stage, stage_it = 0, 0
+        stage_tol = max(opts.stage_tol, 1e-5)              # float32 floors (sinkhorn.py:342-344)
+        tol = max(opts.tol, 5e-6) if not balanced else opts.tol
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        while it < opts.max_iters:
+            if stages:
+                e = stages[stage] if stage < len(stages) else opts.eps
+            else:
+                e = sched[it] if it < len(sched) else opts.eps
+            inv_eps = float(np.float32(1.0 / e))
+            step(X, Y, gh, e, kap(e, rho_x), out=fh)
+            gh_new = bufs[it % 2] if bufs[it % 2] is not gh else bufs[(it + 1) % 2]
+            step(Y, X, fh, e, kap(e, rho_y), out=gh_new)
+            it += 1
+            stage_it += 1
+            if stages and stage < len(stages):
+                if stage_it % opts.check_every == 0:
+                    _capi.max_change(gh, gh_new, Y.n, inv_eps, err_dev)
+                    ch = float(err_dev.item())
+                    if ch < stage_tol or stage_it >= opts.stage_max_iters:
+                        stage, stage_it = stage + 1, 0
+                gh = gh_new
+                continue
+            check = (not opts.fixed_iters and (stages or it > len(sched))
+                     and (stage_it % opts.check_every == 0 or it == opts.max_iters))
+            if check:
+                if balanced:
+                    _capi.balanced_error(gh, gh_new, Y.w, Y.npad, inv_eps, err_dev)
+                else:
+                    _capi.max_change(gh, gh_new, Y.n, inv_eps, err_dev)
+                err = float(err_dev.item())
+            gh = gh_new
+            if check and err < tol:
+                converged = True
+                break
+        f = fh[:X.n].to(torch.float64).cpu().numpy() + X.sq64[:X.n]
+        g = gh[:Y.n].to(torch.float64).cpu().numpy() + Y.sq64[:Y.n]
+        row_mass = col_mass = None
+        if not balanced:
+            # The plan's marginals from one balanced (kappa = 1, no offset) update each way (sinkhorn.py:381-389).
+            fb = step(X, Y, gh, opts.eps, 1.0, use_off=False)[:X.n].to(torch.float64).cpu().numpy() + X.sq64[:X.n]
+            gb = step(Y, X, fh, opts.eps, 1.0, use_off=False)[:Y.n].to(torch.float64).cpu().numpy() + Y.sq64[:Y.n]
+            row_mass = np.exp(log_a + (f - fb) / opts.eps)
+            col_mass = np.exp(log_b + (g - gb) / opts.eps)
+        flags = _capi.device_error_flags()
+        if flags:
+            raise _capi.TrnoptError(f"a kernel reported device error flags {flags:#x} during the solve")
+        seconds = time.perf_counter() - t0
+    cost = float(np.exp(log_a) @ f + np.exp(log_b) @ g) if balanced else float("nan")
+    return SinkhornResult(f=f, g=g, iterations=it, error=err, converged=converged, cost=cost, seconds=seconds,
+                          eps=opts.eps, rho=opts.rho, center=center, cost_scale=scale, row_mass=row_mass,
+                          col_mass=col_mass)
+
+
+def transport_plan(x, y, res: SinkhornResult, a=None, b=None) -> np.ndarray:
+    """The dense plan P (n x m, float64) from a result, on the host: for small problems and tests only
+    (sinkhorn.py:397-403)."""
+    x = (np.asarray(x, dtype=np.float64) - res.center) / np.sqrt(res.cost_scale)
+    y = (np.asarray(y, dtype=np.float64) - res.center) / np.sqrt(res.cost_scale)
+    log_a, log_b = _log_weights(a, len(x), "a"), _log_weights(b, len(y), "b")
+    C = ((x[:, None, :] - y[None, :, :]) ** 2).sum(axis=2)
+    return np.exp(log_a[:, None] + log_b[None, :] + (res.f[:, None] + res.g[None, :] - C) / res.eps)
