@@ -207,7 +207,7 @@ def run_ours(args, rank, world, dev):
     S = sys.modules["trnopt.sinkhorn"]
     name, x, y, kw, cfg = workload(args.workload, world)
     eps = kw["eps"]
-    path = S._resolve_path(args.path, x.shape[1]) if hasattr(S, "_resolve_path") else "ffma"
+    path = S._resolve_path(args.path, x.shape[1])
     if kw["normalize"]:
         center, scale = S.normalization(x, y, how="mean")
     else:
@@ -219,10 +219,9 @@ def run_ours(args, rank, world, dev):
     la, lb = np.full(n, -np.log(n)), np.full(m, -np.log(m))
     X = S._Cloud(xi, la, world, dev)
     Y = S._Cloud(yi, lb, world, dev)
-    if hasattr(S, "_prepare_path"):
-        S._prepare_path(path, X, Y)
-    ws = S._workspace(X, Y, world, dev, path) if path != "ffma" else S._workspace(X, Y, world, dev)
-    step = S._CudaStep(dev, world, rank, ws, path=path) if path != "ffma" else S._CudaStep(dev, world, rank, ws)
+    S._prepare_path(path, X, Y)
+    ws = S._workspace(X, Y, world, dev, path)
+    step = S._CudaStep(dev, world, rank, ws, path=path)
     gh = torch.zeros(Y.npad, dtype=torch.float32, device=dev)
     fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -295,9 +294,9 @@ def run_ours(args, rank, world, dev):
     e2e = None
     if not args.no_e2e:
         opts = SinkhornOptions(max_iters=args.steps, fixed_iters=True, backend=Backend.preset("cuda-fused", device=str(dev)),
-                               cores=world, **({"cuda_path": path} if path != "ffma" else {}), **kw)
+                               cores=world, cuda_path=path, **kw)
         sinkhorn(x[:256], y[:256], opts=SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend,
-                                                         cores=world, **kw))
+                                                         cores=world, cuda_path=path, **kw))
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)

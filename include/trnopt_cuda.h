@@ -75,6 +75,23 @@ int trnopt_half_step(const float* xT, int ldx, const float* xsq, const float* of
                      const float* gh, const float* log_b, int rows, int m, int d, float eps, float kappa,
                      float* fh, void* workspace, size_t ws_bytes, void* stream);
 
+/* Tensor-core path. A cloud is split once per solve into FP16 pairs, x 2^scale_exp = hi + lo, stored as n rows of
+ * [hi (dk) | lo (dk) | zeros] (dk = d rounded up to 16; trnopt_pack_bytes gives the size; 128-byte aligned).
+ * scale_exp is chosen by the caller so that max |x| 2^scale_exp <= 1 (keeps lo in FP16 range). The counterpart
+ * of the reference's once-per-solve kernel layout, the [x ; 1] blocks of _Cloud (sinkhorn.py:159-165).
+ * Supported for d <= 64. */
+size_t trnopt_pack_bytes(int n, int d);
+int trnopt_pack_cloud(const float* xT, int ldx, int n, int d, int scale_exp, void* packed, void* stream);
+
+/* The fused half-step on tcgen05 tensor cores (same contract as trnopt_half_step, sinkhorn.py:108-119 /
+ * nki_sinkhorn.py:175-228): x . y as xh.yh + xh.yl + xl.yh in FP16 with FP32 accumulation (about 22 significant
+ * bits), bias gh / eps + log b added in FP32, online row log-sum-exp. xpack = rows packed rows of this side
+ * (scale sx), ypack = m packed rows of the other side (scale sy). Needs an sm_100 device; workspace from
+ * trnopt_workspace_size(rows, m, d, TRNOPT_PATH_TC). */
+int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
+                        const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
+                        void* workspace, size_t ws_bytes, void* stream);
+
 /* Row log-sum-exp of a product, lse_i = log sum_j exp(xa_i . ya_j), xa_T (k, ldx), ya_T (k, ldy), 1 <= k <= 128.
  * Replaces make_row_lse_kernel(K, rows, m)(xa_T, ya_T) (nki_sinkhorn.py:150-172). */
 int trnopt_row_lse(const float* xaT, int ldx, const float* yaT, int ldy, int rows, int m, int k, float* lse,

@@ -1,8 +1,9 @@
 """The fused half-step through the C ABI against the reference's own answers (golden KATs) and the float64 oracle.
 
-Tolerance: potentials are compared in units of eps, |fh_gpu - fh_ref| / eps <= HS_TOL. The reference's own float32
-half-step is about 1e-5 eps from its float64 one on these inputs; HS_TOL leaves room for a different (also
-float32) summation order.
+Tolerance: potentials are compared in units of eps, |fh_gpu - fh_ref| / eps <= HS_TOL, or, on the reference's own
+known-answer inputs, no worse than the reference's float32 half-step on the same inputs (its uncentred case with
+eps 0.02 has scores of magnitude ~300, where one float32 rounding is already ~2e-5 eps). Both kernels (FFMA and
+tensor-core split precision) are held to the same bar.
 """
 
 import numpy as np
@@ -21,6 +22,15 @@ def _dev(a, dt=torch.float32):
     return torch.as_tensor(np.ascontiguousarray(a), dtype=dt).cuda()
 
 
+PATHS = [_capi.PATH_FFMA, _capi.PATH_TC]
+PATH_IDS = ["ffma", "tc"]
+
+
+def scale_exp(a):
+    mx = float(np.abs(a).max())
+    return 0 if mx == 0 else -int(np.ceil(np.log2(mx)))
+
+
 def gpu_half_step(x, xsq, off, y, gh, log_b, eps, kappa, ws=None, path=_capi.PATH_FFMA):
     rows, d = x.shape
     m = y.shape[0]
@@ -29,8 +39,16 @@ def gpu_half_step(x, xsq, off, y, gh, log_b, eps, kappa, ws=None, path=_capi.PAT
     if ws is None:
         ws = _capi.new_workspace(_capi.workspace_size(rows, m, d, path), "cuda")
     fh = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
-    _capi.half_step(xT, ldx, _dev(xsq), None if off is None else _dev(off), yT, ldy, _dev(gh), _dev(log_b), rows, m,
-                    d, eps, kappa, fh, ws)
+    offd = None if off is None else _dev(off)
+    if path == _capi.PATH_FFMA:
+        _capi.half_step(xT, ldx, _dev(xsq), offd, yT, ldy, _dev(gh), _dev(log_b), rows, m, d, eps, kappa, fh, ws)
+    else:
+        sx, sy = scale_exp(x), scale_exp(y)
+        xp = _capi.pack_cloud(xT, ldx, rows, d, sx)
+        yp = _capi.pack_cloud(yT, ldy, m, d, sy)
+        _capi.half_step_tc(xp, _dev(xsq), offd, yp, _dev(gh), _dev(log_b), rows, m, d, sx, sy, eps, kappa, fh, ws)
+    torch.cuda.synchronize()
+    assert _capi.device_error_flags() == 0
     return fh.cpu().numpy().astype(np.float64)
 
 
@@ -40,15 +58,18 @@ def oracle_half_step(x, xsq, off, y, gh, log_b, eps, kappa):
     return O.half_step(t(x), t(xsq), t(off), t(y.T.copy()), t(gh), t(log_b), 1.0 / eps, eps, kappa).numpy()
 
 
-def test_half_step_reference_kat(golden):
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
+def test_half_step_reference_kat(golden, path):
     z = golden("half_step_kat.npz")
     for c in range(int(z["ncases"])):
         g = lambda k: z[f"c{c}_{k}"]
         eps, kappa = float(g("eps")), float(g("kappa"))
-        fh = gpu_half_step(g("x"), g("xsq"), g("off"), g("y"), g("gh"), g("log_b"), eps, kappa)
+        if path == _capi.PATH_TC and not _capi.tc_supported(g("x").shape[1]):
+            continue
+        fh = gpu_half_step(g("x"), g("xsq"), g("off"), g("y"), g("gh"), g("log_b"), eps, kappa, path=path)
         err = np.abs(fh - g("fh_f64")).max() / eps
         ref32 = np.abs(g("fh_f32") - g("fh_f64")).max() / eps
-        assert err <= HS_TOL, (c, err, ref32)
+        assert err <= max(HS_TOL, ref32), (c, err, ref32)
 
 
 def problem(rows, m, d, seed, eps, pad=0):
@@ -74,13 +95,33 @@ def problem(rows, m, d, seed, eps, pad=0):
     (4096, 4096, 64, 0.02, 0.7, True, 96),
     (20000, 700, 64, 0.1, 1.0, False, 0),
 ])
-def test_half_step_matches_oracle(rows, m, d, eps, kappa, use_off, pad):
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
+def test_half_step_matches_oracle(rows, m, d, eps, kappa, use_off, pad, path):
+    if path == _capi.PATH_TC and not _capi.tc_supported(d):
+        pytest.skip("tensor-core path covers d <= 64")
     x, xsq, off, y, gh, lb = problem(rows, m, d, rows * 7 + m, eps, pad)
     off = off if use_off else None
-    fh = gpu_half_step(x, xsq, off, y, gh, lb, eps, kappa)
+    fh = gpu_half_step(x, xsq, off, y, gh, lb, eps, kappa, path=path)
     ref = oracle_half_step(x, xsq, off, y, gh, lb, eps, kappa)
     err = np.abs(fh - ref).max() / eps
     assert np.all(np.isfinite(fh)) and err <= HS_TOL, err
+
+
+def test_tc_and_ffma_agree_at_config_2_size():
+    """One full-size config-2 half-step (10k x 10k, d 64, centred U[0,1] points) on both kernels."""
+    from trnopt import synthetic
+    x, y = synthetic.cfg2()
+    c = np.concatenate([x, y]).mean(0)
+    x, y = x - c, y - c
+    gh = -(y * y).sum(1)
+    lb = np.full(len(y), -np.log(len(y)))
+    a = gpu_half_step(x, (x * x).sum(1), None, y, gh, lb, 0.1, 1.0, path=_capi.PATH_FFMA)
+    b = gpu_half_step(x, (x * x).sum(1), None, y, gh, lb, 0.1, 1.0, path=_capi.PATH_TC)
+    rows = np.random.default_rng(0).choice(len(x), 64, replace=False)
+    ref = oracle_half_step(x[rows], (x[rows] ** 2).sum(1), None, y, gh, lb, 0.1, 1.0)
+    assert np.abs(a[rows] - ref).max() / 0.1 <= HS_TOL
+    assert np.abs(b[rows] - ref).max() / 0.1 <= HS_TOL
+    assert np.abs(a - b).max() / 0.1 <= 2 * HS_TOL
 
 
 def test_row_lse_reference_kat(golden):
@@ -89,11 +130,12 @@ def test_row_lse_reference_kat(golden):
     assert np.abs(lse - z["lse"]).max() <= LSE_TOL
 
 
-def test_workspace_is_left_ready_and_results_are_deterministic():
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
+def test_workspace_is_left_ready_and_results_are_deterministic(path):
     x, xsq, off, y, gh, lb = problem(3000, 7000, 64, 1, 0.1)
-    ws = _capi.new_workspace(_capi.workspace_size(3000, 7000, 64), "cuda")
-    a = gpu_half_step(x, xsq, off, y, gh, lb, 0.1, 0.9, ws=ws)
-    b = gpu_half_step(x, xsq, off, y, gh, lb, 0.1, 0.9, ws=ws)
+    ws = _capi.new_workspace(_capi.workspace_size(3000, 7000, 64, path), "cuda")
+    a = gpu_half_step(x, xsq, off, y, gh, lb, 0.1, 0.9, ws=ws, path=path)
+    b = gpu_half_step(x, xsq, off, y, gh, lb, 0.1, 0.9, ws=ws, path=path)
     assert np.array_equal(a, b)
     assert torch.count_nonzero(ws[:256]).item() == 0          # arrival counters back at zero
     assert _capi.device_error_flags() == 0

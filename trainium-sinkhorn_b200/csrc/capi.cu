@@ -112,6 +112,10 @@ size_t trnopt_workspace_size(int rows, int m, int d, int path) {
   if (path == TRNOPT_PATH_FFMA) {
     ffma_plan(current_device(), rows, m, d, sk);
     partial = ffma_partial_bytes(sk);
+  } else if (path == TRNOPT_PATH_TC) {
+    if (!tc_supported_d(d)) return 0;
+    tc_plan(current_device(), rows, m, d, sk);
+    partial = tc_partial_bytes(sk);
   } else {
     return 0;
   }
@@ -154,6 +158,46 @@ int trnopt_row_lse(const float* xaT, int ldx, const float* yaT, int ldy, int row
   p.xT = xaT; p.ldx = ldx; p.yT = yaT; p.ldy = ldy; p.rows = rows; p.m = m; p.d = k;
   p.dot2 = kLog2e; p.gh2 = 0.f; p.lb2 = 0.f; p.eps = 1.0; p.kappa = 1.0; p.mode = 1; p.out = lse;
   return ffma_run(p, workspace, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t trnopt_pack_bytes(int n, int d) {
+  if (n < 1 || !tc_supported_d(d)) return 0;
+  return (size_t)n * tc_kp(d) * 2;
+}
+
+int trnopt_pack_cloud(const float* xT, int ldx, int n, int d, int scale_exp, void* packed, void* stream) {
+  if (!tc_supported_d(d)) return TRNOPT_ERR_UNSUPPORTED;
+  int st = check_points(xT, ldx, n, d);
+  if (st != TRNOPT_OK) return st;
+  if (packed == nullptr || scale_exp < -100 || scale_exp > 100) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned(packed, 128)) return TRNOPT_ERR_ALIGNMENT;
+  return cuda_status(tc_pack(xT, ldx, n, d, scale_exp, packed, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
+                        const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
+                        void* workspace, size_t ws_bytes, void* stream) {
+  if (!tc_supported_d(d)) return TRNOPT_ERR_UNSUPPORTED;
+  if (!xpack || !ypack || !xsq || !gh || !log_b || !fh || rows < 1 || m < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned(xpack, 128) || !aligned(ypack, 128)) return TRNOPT_ERR_ALIGNMENT;
+  if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return TRNOPT_ERR_UNSUPPORTED;
+  LseProblem p{};
+  p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off; p.rows = rows; p.m = m; p.d = d;
+  const double inv_eps = 1.0 / (double)eps;
+  p.dot2 = (float)(2.0 * inv_eps * 1.4426950408889634);
+  p.gh2 = (float)(inv_eps * 1.4426950408889634);
+  p.lb2 = kLog2e;
+  p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
+  StreamK sk{};
+  tc_plan(dev, rows, m, d, sk);
+  int st = bind_workspace(sk, tc_partial_bytes(sk), workspace, ws_bytes);
+  if (st != TRNOPT_OK) return st;
+  p.error_word = device_error_word();
+  return cuda_status(tc_launch(p, xpack, ypack, sx, sy, sk, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 size_t trnopt_median_workspace_size(void) { return median_workspace_bytes(); }

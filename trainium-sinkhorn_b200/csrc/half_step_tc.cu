@@ -1,0 +1,563 @@
+// Fused Sinkhorn half-step on the 5th-generation tensor cores (tcgen05, sm_100a), split precision.
+//
+// The contraction x_i . y_j runs as three FP16 tensor-core products with FP32 accumulation in tensor memory,
+//     x . y ~= 2^-(sx+sy) * ( xh . yh + xh . yl + xl . yh ),   x 2^sx = xh + xl,  y 2^sy = yh + yl  (FP16 pairs)
+// where the power-of-two scales put each cloud's largest coordinate at magnitude <= 1 and the low halves carry
+// the next 11 bits, so the products keep about 22 significant bits (FP32-level; a plain FP16 or TF32 product
+// keeps 11, which moves plans by percents -- the reference's README reports 2-3.5% for TF32). The points do not
+// change during a solve, so each cloud is split once (tc_pack) into rows of [hi (dk) | lo (dk)] FP16 values.
+//
+// Per CTA (one per SM, persistent over a stream-K range of (128-row tile, 256-column tile) units):
+//   warp 8      TMA producer: row tiles (A, two buffers) and column tiles (B, a ring of stages) into 128B-swizzled
+//               shared memory; its lanes also write the tile's column bias (gh / eps + log b) * log2(e) to a ring.
+//   warp 9      allocates 512 TMEM columns and issues the MMAs (M 128, N 256, K 16; 3 dk / 16 per tile) into one
+//               of two 128 x 256 FP32 accumulators, committing to mbarriers.
+//   warps 0-7   two epilogue warpgroups, one per accumulator: each thread owns one row, reads its 256 scores of a
+//               tile from TMEM 32 at a time, adds the bias in FP32 and folds them into an online (max, sum) in
+//               base 2 (MUFU ex2). At the end of a segment each warpgroup writes its partial; the last arrival for
+//               a row tile merges all partials and writes fh (common.cuh).
+// Every mbarrier wait is bounded (common.cuh kWaitLimitNs); a timeout sets the device error word and the CTA
+// unwinds (waits for its own copies and MMAs, frees TMEM) instead of hanging.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace trnopt {
+
+constexpr int TC_BM = 128;          // rows per tile (MMA M, TMEM lanes)
+constexpr int TC_BN = 256;          // columns per tile (MMA N)
+constexpr int TC_THREADS = 320;     // 8 epilogue warps + producer + MMA
+constexpr int TC_NBIAS = 4;         // bias ring slots
+constexpr int TC_PRODUCER_WARP = 8;
+constexpr int TC_MMA_WARP = 9;
+
+// ------------------------------------------------------------------------------------------------------------
+// PTX wrappers
+// ------------------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: spin on try_wait; every 256 polls look at the clock and (unless draining) at the CTA's abort flag.
+// Draining waits (for our own copies and MMAs before exit) ignore the abort flag but keep the time limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error_word,
+                                          bool draining = false) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (!draining && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicOr(error_word, (int)kErrWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+#define TRNOPT_TMEM_LD32(taddr, v)                                                                               \
+  asm volatile(                                                                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, " \
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"              \
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),          \
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),    \
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),  \
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])   \
+      : "r"(taddr)                                                                                               \
+      : "memory")
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte swizzle layout: rows of 128 bytes,
+// 8-row atoms of 1024 bytes stacked along M/N (stride byte offset 1024), start address in 16-byte units.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);          // start address
+  d |= (uint64_t)1u << 16;                           // leading byte offset (unused with swizzling; 16 B)
+  d |= (uint64_t)(1024u >> 4) << 32;                 // stride byte offset: 1024 B between 8-row groups
+  d |= (uint64_t)1u << 46;                           // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;                           // layout: 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D F32, A and B FP16, both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+                            ((uint32_t)(TC_BM >> 4) << 24);
+
+// ------------------------------------------------------------------------------------------------------------
+// The kernel
+// ------------------------------------------------------------------------------------------------------------
+
+template <int NKB>
+struct TcCfg {
+  static constexpr int A_BYTES = NKB * TC_BM * 128;      // one row tile: NKB K-blocks of 128 rows x 128 B
+  static constexpr int B_BYTES = NKB * TC_BN * 128;      // one column tile
+  static constexpr int NS = NKB == 1 ? 4 : 2;            // column-tile stages
+  static constexpr int OFF_B = 2 * A_BYTES;
+  static constexpr int OFF_BIAS = OFF_B + NS * B_BYTES;
+  static constexpr int OFF_BAR = OFF_BIAS + TC_NBIAS * TC_BN * 4;
+  // barriers: full[NS], empty[NS], a_full[2], a_empty[2], acc_full[2], acc_empty[2], bias_full[NB], bias_empty[NB],
+  // drain[1]
+  static constexpr int NBAR = 2 * NS + 8 + 2 * TC_NBIAS + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 64 + 1024;     // + alignment slack for the 1024-byte aligned base
+};
+
+struct TcArgs {
+  LseProblem p;
+  StreamK sk;
+  int dk;            // elements of each half (hi, lo) per packed row; multiple of 16
+};
+
+template <int NKB>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    half_step_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const TcArgs args) {
+  using C = TcCfg<NKB>;
+  extern __shared__ uint8_t tc_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  const LseProblem& p = args.p;
+  const StreamK& sk = args.sk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full_b = bars;
+  uint64_t* empty_b = bars + C::NS;
+  uint64_t* a_full = bars + 2 * C::NS;
+  uint64_t* a_empty = a_full + 2;
+  uint64_t* acc_full = a_empty + 2;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* bias_full = acc_empty + 2;
+  uint64_t* bias_empty = bias_full + TC_NBIAS;
+  uint64_t* drain = bias_empty + TC_NBIAS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+  int* s_last = reinterpret_cast<int*>(smem + C::OFF_MISC + 16);     // [2], one per epilogue warpgroup
+  float* bias_ring = reinterpret_cast<float*>(smem + C::OFF_BIAS);
+
+  if (blockDim.x != TC_THREADS) {
+    if (threadIdx.x == 0) atomicOr(p.error_word, (int)kErrBadLaunch);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NS; ++s) { mbar_init(&full_b[s], 1); mbar_init(&empty_b[s], 1); }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&a_full[b], 1); mbar_init(&a_empty[b], 1);
+      mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 128);
+    }
+    for (int s = 0; s < TC_NBIAS; ++s) { mbar_init(&bias_full[s], 32); mbar_init(&bias_empty[s], 128); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == TC_MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp == TC_PRODUCER_WARP && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const long long u_begin = sk_unit_begin(blockIdx.x, sk.units, sk.grid);
+  const long long u_end = sk_unit_begin(blockIdx.x + 1, sk.units, sk.grid);
+  const int dk = args.dk;
+  const int ksteps = dk / 16;
+
+  if (warp == TC_PRODUCER_WARP) {
+    // ---------------------------------------------------------------- producer
+    int T = 0, seg = 0, seg_issued = 0;
+    bool ok = true, issued_current = false;
+    for (long long u = u_begin; u < u_end && ok; ++seg) {
+      const int r = (int)(u / sk.nct);
+      const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
+      const int a_slot = seg & 1;
+      ok = mbar_wait(&a_empty[a_slot], ((seg >> 1) & 1) ^ 1, abort_flag, p.error_word);
+      if (!ok) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&a_full[a_slot], C::A_BYTES);
+        for (int kb = 0; kb < NKB; ++kb)
+          tma_load_2d(smem + a_slot * C::A_BYTES + kb * TC_BM * 128, &map_a, &a_full[a_slot], kb * 64, r * TC_BM);
+      }
+      seg_issued = seg + 1;
+      for (; u < seg_end; ++u, ++T) {
+        const int c = (int)(u % sk.nct);
+        const int stage = T % C::NS;
+        issued_current = false;
+        ok = mbar_wait(&empty_b[stage], ((T / C::NS) & 1) ^ 1, abort_flag, p.error_word);
+        if (!ok) break;
+        issued_current = true;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full_b[stage], C::B_BYTES);
+          for (int kb = 0; kb < NKB; ++kb)
+            tma_load_2d(smem + C::OFF_B + stage * C::B_BYTES + kb * TC_BN * 128, &map_b, &full_b[stage], kb * 64,
+                        c * TC_BN);
+        }
+        const int bslot = T % TC_NBIAS;
+        ok = mbar_wait(&bias_empty[bslot], ((T / TC_NBIAS) & 1) ^ 1, abort_flag, p.error_word);
+        if (!ok) break;
+        float* bias = bias_ring + bslot * TC_BN;
+#pragma unroll
+        for (int q = 0; q < TC_BN / 32; ++q) {
+          const int jj = q * 32 + lane;
+          const int j = c * TC_BN + jj;
+          float b = -INFINITY;
+          if (j < p.m) b = fmaf(p.log_b[j], p.lb2, p.gh[j] * p.gh2);
+          bias[jj] = b;
+        }
+        mbar_arrive(&bias_full[bslot]);
+      }
+    }
+    // Unwind: make sure no copy of ours is still landing in shared memory when the CTA exits. Stage s has had
+    // ceil((issued - s) / NS) fills; the last one completes phase (fills - 1).
+    if (!ok && lane == 0) {
+      const int issued = T + (issued_current ? 1 : 0);
+      for (int s = 0; s < C::NS; ++s) {
+        const int fills = (issued - s + C::NS - 1) / C::NS;
+        if (fills > 0) mbar_wait(&full_b[s], (uint32_t)((fills - 1) & 1), abort_flag, p.error_word, true);
+      }
+      for (int a = 0; a < 2; ++a) {
+        const int fills = (seg_issued - a + 1) / 2;
+        if (fills > 0) mbar_wait(&a_full[a], (uint32_t)((fills - 1) & 1), abort_flag, p.error_word, true);
+      }
+    }
+  } else if (warp == TC_MMA_WARP) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int T = 0, seg = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(smem);
+      const uint32_t b_base = smem_u32(smem + C::OFF_B);
+      for (long long u = u_begin; u < u_end && ok; ++seg) {
+        const int r = (int)(u / sk.nct);
+        const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
+        const int a_slot = seg & 1;
+        ok = mbar_wait(&a_full[a_slot], (seg >> 1) & 1, abort_flag, p.error_word);
+        if (!ok) break;
+        for (; u < seg_end; ++u, ++T) {
+          const int stage = T % C::NS;
+          const int acc = T & 1;
+          ok = mbar_wait(&acc_empty[acc], ((T >> 1) & 1) ^ 1, abort_flag, p.error_word);
+          if (ok) ok = mbar_wait(&full_b[stage], (T / C::NS) & 1, abort_flag, p.error_word);
+          if (!ok) break;
+          tmem_fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TC_BN);
+          const uint32_t a_tile = a_base + a_slot * C::A_BYTES;
+          const uint32_t b_tile = b_base + stage * C::B_BYTES;
+          uint32_t accumulate = 0;
+#pragma unroll
+          for (int pass = 0; pass < 3; ++pass) {
+            const int ea0 = (pass == 2) ? dk : 0;              // hi.hi, hi.lo, lo.hi
+            const int eb0 = (pass == 1) ? dk : 0;
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const int ea = ea0 + 16 * kk, eb = eb0 + 16 * kk;
+              const uint32_t sa = a_tile + (ea >> 6) * (TC_BM * 128) + (ea & 63) * 2;
+              const uint32_t sb = b_tile + (eb >> 6) * (TC_BN * 128) + (eb & 63) * 2;
+              umma_f16(d_tmem, sw128_desc(sa), sw128_desc(sb), kIdesc, accumulate);
+              accumulate = 1;
+            }
+          }
+          umma_commit(&empty_b[stage]);
+          umma_commit(&acc_full[acc]);
+        }
+        if (ok) umma_commit(&a_empty[a_slot]);
+      }
+      // Wait for every MMA we issued before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, abort_flag, p.error_word, true);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue warpgroups 0 and 1
+    const int wg = warp >> 2;                  // which accumulator / which tiles (T % 2 == wg)
+    const int qrow = (warp & 3) * 32 + lane;   // this thread's row in the tile == its TMEM lane
+    const uint32_t lane_addr = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(wg * TC_BN);
+    const float dot2 = p.dot2;
+    int T = 0;
+    bool ok = true;
+    for (long long u = u_begin; u < u_end;) {
+      const int r = (int)(u / sk.nct);
+      const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
+      float M = kMaxFloor, L = 0.f;
+      for (; u < seg_end; ++u, ++T) {
+        if ((T & 1) != wg || !ok) continue;
+        ok = mbar_wait(&acc_full[wg], (T >> 1) & 1, abort_flag, p.error_word);
+        const int bslot = T % TC_NBIAS;
+        if (ok) ok = mbar_wait(&bias_full[bslot], (T / TC_NBIAS) & 1, abort_flag, p.error_word);
+        if (!ok) continue;
+        tmem_fence_after();
+        const float* bias = bias_ring + bslot * TC_BN;
+        uint32_t v[32];
+        TRNOPT_TMEM_LD32(lane_addr, v);
+        tmem_wait_ld();
+#pragma unroll 1
+        for (int ch = 0; ch < TC_BN / 32; ++ch) {
+          float t[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            asm volatile("" : "+r"(v[j]));
+            t[j] = __uint_as_float(v[j]);
+          }
+          if (ch + 1 < TC_BN / 32) TRNOPT_TMEM_LD32(lane_addr + (uint32_t)((ch + 1) * 32), v);
+          const float4* b4 = reinterpret_cast<const float4*>(bias + ch * 32);
+          float cmax = kMaxFloor;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 b = b4[q];
+            t[4 * q + 0] = fmaf(t[4 * q + 0], dot2, b.x);
+            t[4 * q + 1] = fmaf(t[4 * q + 1], dot2, b.y);
+            t[4 * q + 2] = fmaf(t[4 * q + 2], dot2, b.z);
+            t[4 * q + 3] = fmaf(t[4 * q + 3], dot2, b.w);
+            cmax = fmaxf(cmax, fmaxf(fmaxf(t[4 * q], t[4 * q + 1]), fmaxf(t[4 * q + 2], t[4 * q + 3])));
+          }
+          if (cmax > M) {
+            L *= ex2_approx(M - cmax);
+            M = cmax;
+          }
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            s0 += ex2_approx(t[j] - M);
+            s1 += ex2_approx(t[j + 1] - M);
+          }
+          L += s0 + s1;
+          if (ch + 1 < TC_BN / 32) tmem_wait_ld();
+        }
+        tmem_fence_before();
+        mbar_arrive(&acc_empty[wg]);
+        mbar_arrive(&bias_empty[bslot]);
+      }
+      // Segment done: this warpgroup's partial for row tile r, then one arrival on the row tile's counter.
+      const long long first_u = (long long)r * sk.nct;
+      const int kfirst = sk_cta_of(first_u, sk.units, sk.grid);
+      const int klast = sk_cta_of(first_u + sk.nct - 1, sk.units, sk.grid);
+      const int expected = 2 * (klast - kfirst + 1);
+      const int slot = 2 * (blockIdx.x - kfirst) + wg;
+      float2* base = sk.partials + (size_t)r * sk.slots * TC_BM;
+      base[(size_t)slot * TC_BM + qrow] = make_float2(M, L);
+      __threadfence();
+      asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+      if (qrow == 0) {
+        const int old = atomicAdd(&sk.counters[r], 1);
+        s_last[wg] = (old == expected - 1);
+      }
+      asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+      if (s_last[wg]) {
+        __threadfence();
+        const int row = r * TC_BM + qrow;
+        if (row < p.rows) finish_row(p, row, base + qrow, expected, TC_BM);
+        if (qrow == 0) sk.counters[r] = 0;
+      }
+    }
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == TC_MMA_WARP) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Packing: rows of [hi (dk) | lo (dk) | zero padding to kp] in FP16 from transposed FP32 points.
+// ------------------------------------------------------------------------------------------------------------
+
+__global__ void tc_pack_kernel(const float* __restrict__ xT, int ldx, int n, int d, int dk, int kp, float scale,
+                               __half* __restrict__ out) {
+  const long long total = (long long)n * kp;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(idx / kp), k = (int)(idx % kp);
+    __half h = __float2half_rn(0.f);
+    const int kk = k < dk ? k : k - dk;
+    if (k < 2 * dk && kk < d) {
+      const float v = xT[(size_t)kk * ldx + i] * scale;     // exact: scale is a power of two
+      const __half hi = __float2half_rn(v);
+      h = (k < dk) ? hi : __float2half_rn(v - __half2float(hi));
+    }
+    out[idx] = h;
+  }
+}
+
+int tc_dk(int d) { return (d + 15) / 16 * 16; }
+int tc_kp(int d) { return (2 * tc_dk(d) + 63) / 64 * 64; }
+int tc_supported_d(int d) { return (d >= 1 && tc_kp(d) <= 128) ? tc_dk(d) : 0; }
+
+cudaError_t tc_pack(const float* xT, int ldx, int n, int d, int scale_exp, void* packed, cudaStream_t stream) {
+  const int dk = tc_dk(d), kp = tc_kp(d);
+  const long long total = (long long)n * kp;
+  const int threads = 256;
+  const long long blocks = (total + threads - 1) / threads;
+  const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
+  tc_pack_kernel<<<grid, threads, 0, stream>>>(xT, ldx, n, d, dk, kp, ldexpf(1.0f, scale_exp),
+                                               reinterpret_cast<__half*>(packed));
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Host side: tensor maps (cached per pointer / shape), planning, launch
+// ------------------------------------------------------------------------------------------------------------
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+struct MapEntry {
+  const void* ptr;
+  int rows, kp, box_rows;
+  CUtensorMap map;
+};
+constexpr int kMapCache = 32;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+std::mutex g_map_mutex;
+
+bool tensor_map(const void* ptr, int rows, int kp, int box_rows, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  for (int i = 0; i < kMapCache; ++i) {
+    const MapEntry& e = g_maps[i];
+    if (e.ptr == ptr && e.rows == rows && e.kp == kp && e.box_rows == box_rows) {
+      *out = e.map;
+      return true;
+    }
+  }
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  MapEntry e{ptr, rows, kp, box_rows, {}};
+  const cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kp * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(&e.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  g_maps[g_map_next] = e;
+  g_map_next = (g_map_next + 1) % kMapCache;
+  *out = e.map;
+  return true;
+}
+
+int g_tc_sms[64] = {0};
+
+}  // namespace
+
+void tc_plan(int device, int rows, int m, int d, StreamK& sk) {
+  (void)d;
+  if (device < 0 || device >= 64) device = 0;
+  if (g_tc_sms[device] == 0) cudaDeviceGetAttribute(&g_tc_sms[device], cudaDevAttrMultiProcessorCount, device);
+  sk.nrt = (rows + TC_BM - 1) / TC_BM;
+  sk.nct = (m + TC_BN - 1) / TC_BN;
+  sk.units = (long long)sk.nrt * sk.nct;
+  const long long g = g_tc_sms[device] > 0 ? g_tc_sms[device] : 148;
+  sk.grid = (int)(g < sk.units ? g : sk.units);
+  sk.slots = 2 * sk_max_slots(sk.units, sk.grid, sk.nct);
+  sk.parts_per_cta = 2;
+}
+
+size_t tc_partial_bytes(const StreamK& sk) { return (size_t)sk.nrt * sk.slots * TC_BM * sizeof(float2); }
+
+template <int NKB>
+static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, cudaStream_t stream) {
+  using C = TcCfg<NKB>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(half_step_tc_kernel<NKB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  half_step_tc_kernel<NKB><<<a.sk.grid, TC_THREADS, C::SMEM, stream>>>(ma, mb, a);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,
+                      cudaStream_t stream) {
+  const int kp = tc_kp(p.d);
+  CUtensorMap ma, mb;
+  if (!tensor_map(xpack, p.rows, kp, TC_BM, &ma) || !tensor_map(ypack, p.m, kp, TC_BN, &mb))
+    return cudaErrorInvalidValue;
+  TcArgs a;
+  a.p = p;
+  a.p.dot2 = (float)((double)p.dot2 * ldexp(1.0, -(sx + sy)));
+  a.sk = sk;
+  a.dk = tc_dk(p.d);
+  if (kp == 64) return tc_launch_t<1>(ma, mb, a, stream);
+  return tc_launch_t<2>(ma, mb, a, stream);
+}
+
+}  // namespace trnopt

@@ -17,6 +17,7 @@ cudaError_t ffma_launch(const LseProblem& p, const StreamK& sk, cudaStream_t str
 // tcgen05 split-precision path (half_step_tc.cu)
 struct TcProblem;
 int tc_supported_d(int d);                       // packed K per half (16-element multiple), 0 if unsupported
+int tc_kp(int d);                                // FP16 elements per packed row
 void tc_plan(int device, int rows, int m, int d, StreamK& sk);
 size_t tc_partial_bytes(const StreamK& sk);
 cudaError_t tc_pack(const float* xT, int ldx, int n, int d, int scale_exp, void* packed, cudaStream_t stream);

@@ -43,6 +43,9 @@ _SIGS = {
     "trnopt_row_lse": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "trnopt_balanced_error": (_I, [_P, _P, _P, _I, _F, _P, _P]),
     "trnopt_max_change": (_I, [_P, _P, _I, _F, _P, _P]),
+    "trnopt_pack_bytes": (_Z, [_I, _I]),
+    "trnopt_pack_cloud": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "trnopt_half_step_tc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _Z, _P]),
     "trnopt_median_workspace_size": (_Z, []),
     "trnopt_median_cost": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
 }
@@ -91,6 +94,31 @@ def half_step(xT, ldx, xsq, off, yT, ldy, gh, log_b, rows, m, d, eps, kappa, fh,
     check(lib.trnopt_half_step(_ptr(xT), ldx, _ptr(xsq), _ptr(off), _ptr(yT), ldy, _ptr(gh), _ptr(log_b), rows, m,
                                d, float(eps), float(kappa), _ptr(fh), _ptr(ws), ws.numel(), _stream()),
           "trnopt_half_step")
+
+
+def pack_bytes(n: int, d: int) -> int:
+    return int(lib.trnopt_pack_bytes(n, d))
+
+
+def tc_supported(d: int) -> bool:
+    return pack_bytes(1, d) > 0
+
+
+def pack_cloud(xT: torch.Tensor, ld: int, n: int, d: int, scale_exp: int) -> torch.Tensor:
+    """Split a transposed cloud (d, ld) into the FP16 [hi | lo] rows of the tensor-core path."""
+    nbytes = pack_bytes(n, d)
+    if nbytes == 0:
+        raise ValueError(f"the tensor-core path does not support d = {d}")
+    out = torch.empty(nbytes // 2, dtype=torch.float16, device=xT.device)
+    check(lib.trnopt_pack_cloud(_ptr(xT), ld, n, d, int(scale_exp), _ptr(out), _stream()), "trnopt_pack_cloud")
+    return out
+
+
+def half_step_tc(xpack, xsq, off, ypack, gh, log_b, rows, m, d, sx, sy, eps, kappa, fh, ws) -> None:
+    """Queue the tensor-core fused half-step on packed clouds."""
+    check(lib.trnopt_half_step_tc(_ptr(xpack), _ptr(xsq), _ptr(off), _ptr(ypack), _ptr(gh), _ptr(log_b), rows, m, d,
+                                  int(sx), int(sy), float(eps), float(kappa), _ptr(fh), _ptr(ws), ws.numel(),
+                                  _stream()), "trnopt_half_step_tc")
 
 
 def row_lse(xaT: torch.Tensor, yaT: torch.Tensor, ws: torch.Tensor | None = None) -> torch.Tensor:

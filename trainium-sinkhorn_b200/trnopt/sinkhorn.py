@@ -56,7 +56,8 @@ class SinkhornOptions:
     cores: int = 1                 # GPUs (torch.distributed ranks) that split each half-step's rows
     kernel: str = "auto"           # "auto" / "cuda": the fused CUDA half-step (the only one in this package)
     backend: Backend = Backend.preset("cuda-fused")
-    cuda_path: str = "ffma"        # "ffma": FP32 FFMA tile kernel
+    cuda_path: str = "auto"        # "tc": tcgen05 split-precision kernel (d <= 64), "ffma": FP32 FFMA tile kernel
+                                   #   (any d <= 128), "auto": tc where it applies
 
 
 @dataclass
@@ -89,6 +90,24 @@ def _use_cuda(opts: SinkhornOptions, d: int) -> None:
         raise ValueError("the fused CUDA half-step supports d <= 128")
     if not torch.cuda.is_available():
         raise RuntimeError("no CUDA device: the fused CUDA half-step has no CPU fallback")
+
+
+def _resolve_path(path: str, d: int) -> str:
+    """Which kernel runs the half-step: the tensor-core one on an sm_100 device for d <= 64, else FFMA."""
+    if path not in ("auto", "tc", "ffma"):
+        raise ValueError(f"cuda_path={path!r}: choose 'auto', 'tc' or 'ffma'")
+    tc_ok = _capi.tc_supported(d) and torch.cuda.is_available() and torch.cuda.get_device_capability()[0] == 10
+    if path == "tc" and not tc_ok:
+        raise ValueError("cuda_path='tc' needs an sm_100 (B200) device and d <= 64")
+    if path == "auto":
+        return "tc" if tc_ok else "ffma"
+    return path
+
+
+def _scale_exp(P: np.ndarray) -> int:
+    """Power-of-two exponent that brings the largest |coordinate| to at most 1 (FP16 split of the TC path)."""
+    mx = float(np.abs(P).max()) if P.size else 0.0
+    return 0 if mx == 0.0 else -int(np.ceil(np.log2(mx)))
 
 
 def _log_weights(w, n: int, name: str) -> np.ndarray:
@@ -150,6 +169,14 @@ class _Cloud:
         self.off = f32(O)
         self.zero = torch.zeros(npad, dtype=torch.float32, device=dev)
         self.h2d_bytes = 4 * (P.size + 4 * npad)
+        self.sexp = _scale_exp(P)
+        self.packed = None
+
+    def pack(self) -> None:
+        """Split the points once into the FP16 [hi | lo] rows of the tensor-core path."""
+        if self.packed is None:
+            self.packed = _capi.pack_cloud(self.xT, self.npad, self.npad, self.d, self.sexp)
+            self.kp = _capi.pack_bytes(1, self.d) // 2
 
 
 class _CudaStep:
@@ -157,8 +184,8 @@ class _CudaStep:
     (P > 1) an all-gather so every rank holds the whole new shifted potential. The counterpart of the reference's
     _NkiStep (sinkhorn.py:177-193)."""
 
-    def __init__(self, dev: torch.device, shards: int, rank: int, ws: torch.Tensor, group=None):
-        self.dev, self.shards, self.rank, self.ws, self.group = dev, shards, rank, ws, group
+    def __init__(self, dev: torch.device, shards: int, rank: int, ws: torch.Tensor, group=None, path: str = "ffma"):
+        self.dev, self.shards, self.rank, self.ws, self.group, self.path = dev, shards, rank, ws, group, path
 
     def rows(self, side: _Cloud) -> tuple[int, int]:
         return _shard_range(side.npad, self.shards, self.rank)
@@ -168,8 +195,13 @@ class _CudaStep:
         out = torch.empty(side.npad, dtype=torch.float32, device=self.dev) if out is None else out
         r0, r1 = self.rows(side)
         off = side.off if use_off else side.zero
-        _capi.half_step(_Off(side.xT, r0), side.npad, _Off(side.sq, r0), _Off(off, r0), other.xT, other.npad,
-                        other_h, other.log_w, r1 - r0, other.npad, side.d, eps, kappa, _Off(out, r0), self.ws)
+        if self.path == "tc":
+            _capi.half_step_tc(_Off(side.packed, r0 * side.kp, 2), _Off(side.sq, r0), _Off(off, r0), other.packed,
+                               other_h, other.log_w, r1 - r0, other.npad, side.d, side.sexp, other.sexp, eps, kappa,
+                               _Off(out, r0), self.ws)
+        else:
+            _capi.half_step(_Off(side.xT, r0), side.npad, _Off(side.sq, r0), _Off(off, r0), other.xT, other.npad,
+                            other_h, other.log_w, r1 - r0, other.npad, side.d, eps, kappa, _Off(out, r0), self.ws)
         if self.shards > 1:
             _gather_rows(out, r0, r1, self.group)
         return out
@@ -190,18 +222,25 @@ def _gather_rows(out: torch.Tensor, r0: int, r1: int, group=None) -> None:
 
 
 class _Off:
-    """A device pointer into a float32 tensor at an element offset (for the ctypes calls)."""
+    """A device pointer into a tensor at an element offset (for the ctypes calls)."""
 
-    def __init__(self, t: torch.Tensor, offset: int):
-        self.t, self.offset = t, offset
+    def __init__(self, t: torch.Tensor, offset: int, itemsize: int = 4):
+        self.t, self.offset, self.itemsize = t, offset, itemsize
 
     def data_ptr(self) -> int:
-        return self.t.data_ptr() + 4 * self.offset
+        return self.t.data_ptr() + self.itemsize * self.offset
 
 
-def _workspace(X: _Cloud, Y: _Cloud, shards: int, dev: torch.device) -> torch.Tensor:
-    need = max(_capi.workspace_size(X.npad // shards, Y.npad, X.d, _capi.PATH_FFMA),
-               _capi.workspace_size(Y.npad // shards, X.npad, X.d, _capi.PATH_FFMA))
+def _prepare_path(path: str, X: _Cloud, Y: _Cloud) -> None:
+    if path == "tc":
+        X.pack()
+        Y.pack()
+
+
+def _workspace(X: _Cloud, Y: _Cloud, shards: int, dev: torch.device, path: str = "ffma") -> torch.Tensor:
+    code = _capi.PATH_TC if path == "tc" else _capi.PATH_FFMA
+    need = max(_capi.workspace_size(X.npad // shards, Y.npad, X.d, code),
+               _capi.workspace_size(Y.npad // shards, X.npad, X.d, code))
     return _capi.new_workspace(need, dev)
 
 
@@ -255,8 +294,10 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
     with torch.cuda.device(dev):
         X = _Cloud(xi, log_a, shards, dev, off_x)
         Y = _Cloud(yi, log_b, shards, dev, off_y)
-        ws = _workspace(X, Y, shards, dev)
-        step = _CudaStep(dev, shards, rank, ws, group)
+        path = _resolve_path(opts.cuda_path, X.d)
+        _prepare_path(path, X, Y)
+        ws = _workspace(X, Y, shards, dev, path)
+        step = _CudaStep(dev, shards, rank, ws, group, path)
 
         sched = []
         stages = [e for e in (opts.eps_stages or ()) if e > opts.eps]
