@@ -77,7 +77,8 @@ int trnopt_half_step(const float* xT, int ldx, const float* xsq, const float* of
 
 /* Tensor-core path. A cloud is split once per solve into FP16 pairs, x 2^scale_exp = hi + lo, stored as n rows of
  * [hi (dk) | lo (dk) | zeros] (dk = d rounded up to 16; trnopt_pack_bytes gives the size; 128-byte aligned).
- * scale_exp is chosen by the caller so that max |x| 2^scale_exp <= 1 (keeps lo in FP16 range). The counterpart
+ * scale_exp is chosen by the caller so that max |x| 2^scale_exp lies in (2^13, 2^14] (hi + lo below FP16's
+ * 65504, low halves of typical coordinates normal FP16 numbers). The counterpart
  * of the reference's once-per-solve kernel layout, the [x ; 1] blocks of _Cloud (sinkhorn.py:159-165).
  * Supported for d <= 64. */
 size_t trnopt_pack_bytes(int n, int d);

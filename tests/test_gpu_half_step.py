@@ -28,7 +28,7 @@ PATH_IDS = ["ffma", "tc"]
 
 def scale_exp(a):
     mx = float(np.abs(a).max())
-    return 0 if mx == 0 else -int(np.ceil(np.log2(mx)))
+    return 0 if mx == 0 else 14 - int(np.ceil(np.log2(mx)))
 
 
 def gpu_half_step(x, xsq, off, y, gh, log_b, eps, kappa, ws=None, path=_capi.PATH_FFMA):

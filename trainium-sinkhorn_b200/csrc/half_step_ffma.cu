@@ -190,10 +190,11 @@ int ffma_grid(int device, int d, long long units) {
     cudaDeviceGetAttribute(&cached_sms, cudaDevAttrMultiProcessorCount, device);
     for (int i = 0; i <= 128; ++i) cached_blocks[i] = 0;
     cached_dev = device;
+    // One opt-in for the largest tile (d = 128): the attribute is a ceiling, every launch asks for its own size.
+    cudaFuncSetAttribute(lse_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ffma_smem_bytes(128));
   }
   if (cached_blocks[d] == 0) {
     const size_t smem = ffma_smem_bytes(d);
-    cudaFuncSetAttribute(lse_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int blocks = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, lse_ffma_kernel, FF_THREADS, smem);
     cached_blocks[d] = blocks > 0 ? blocks : 1;

@@ -2,8 +2,9 @@
 //
 // The contraction x_i . y_j runs as three FP16 tensor-core products with FP32 accumulation in tensor memory,
 //     x . y ~= 2^-(sx+sy) * ( xh . yh + xh . yl + xl . yh ),   x 2^sx = xh + xl,  y 2^sy = yh + yl  (FP16 pairs)
-// where the power-of-two scales put each cloud's largest coordinate at magnitude <= 1 and the low halves carry
-// the next 11 bits, so the products keep about 22 significant bits (FP32-level; a plain FP16 or TF32 product
+// where the power-of-two scales put each cloud's largest coordinate in (2^13, 2^14] (so the low halves of typical
+// coordinates are normal FP16 numbers) and the low halves carry the next 11 bits, so the products keep about
+// 22 significant bits (FP32-level; a plain FP16 or TF32 product
 // keeps 11, which moves plans by percents -- the reference's README reports 2-3.5% for TF32). The points do not
 // change during a solve, so each cloud is split once (tc_pack) into rows of [hi (dk) | lo (dk)] FP16 values.
 //
@@ -306,8 +307,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           uint32_t accumulate = 0;
 #pragma unroll
           for (int pass = 0; pass < 3; ++pass) {
-            const int ea0 = (pass == 2) ? dk : 0;              // hi.hi, hi.lo, lo.hi
-            const int eb0 = (pass == 1) ? dk : 0;
+            // hi.lo and lo.hi first (the small corrections accumulate before the large hi.hi terms), then hi.hi
+            const int ea0 = (pass == 1) ? dk : 0;
+            const int eb0 = (pass == 0) ? dk : 0;
             for (int kk = 0; kk < ksteps; ++kk) {
               const int ea = ea0 + 16 * kk, eb = eb0 + 16 * kk;
               const uint32_t sa = a_tile + (ea >> 6) * (TC_BM * 128) + (ea & 63) * 2;

@@ -105,9 +105,11 @@ def _resolve_path(path: str, d: int) -> str:
 
 
 def _scale_exp(P: np.ndarray) -> int:
-    """Power-of-two exponent that brings the largest |coordinate| to at most 1 (FP16 split of the TC path)."""
+    """Power-of-two exponent that brings the largest |coordinate| into (2^13, 2^14] for the FP16 split of the TC
+    path: high enough that the low halves of typical coordinates stay normal FP16 numbers (11 significant bits;
+    subnormals keep only absolute precision 2^-24), low enough that hi + lo stays below FP16's 65504."""
     mx = float(np.abs(P).max()) if P.size else 0.0
-    return 0 if mx == 0.0 else -int(np.ceil(np.log2(mx)))
+    return 0 if mx == 0.0 else 14 - int(np.ceil(np.log2(mx)))
 
 
 def _log_weights(w, n: int, name: str) -> np.ndarray:
