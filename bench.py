@@ -68,6 +68,65 @@ def workload(name: str, world: int):
     return name, x, y, dict(eps=0.01, normalize="mean"), {"n": len(x), "m": len(y), "d": 64, "eps": 0.01}
 
 
+class NvmlClocks:
+    """SM clock and throttle-reason samples every ~1 ms through NVML while the timed region runs (the region can be a
+    few milliseconds, shorter than nvidia-smi's sampling period). Falls back to nvidia-smi when NVML is missing."""
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+
+    def __init__(self, dev: int, enabled: bool):
+        self.enabled, self.samples, self.reasons, self.max_mhz = enabled, [], set(), None
+        self.stop, self.thread, self.fallback = threading.Event(), None, None
+        if not enabled:
+            return
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.nv, self.h = pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nv, self.fallback = None, Clocks(dev, enabled)
+
+    def _run(self):
+        while True:
+            self._sample()
+            if self.stop.wait(0.001):
+                self._sample()
+                return
+
+    def _sample(self):
+        try:
+            self.samples.append(float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)))
+            mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.reasons.update(k for k, b in self.REASONS.items() if mask & b)
+        except Exception:
+            pass
+
+    def __enter__(self):
+        if self.fallback is not None:
+            self.fallback.__enter__()
+        elif self.enabled:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.fallback is not None:
+            self.fallback.__exit__(*a)
+        elif self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        if self.fallback is not None:
+            return self.fallback.summary()
+        if not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples), "source": "nvml"}
+
+
 class Clocks:
     """nvidia-smi samples of this GPU's SM clock and throttle reasons while the timed region runs."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -241,7 +300,7 @@ def run_ours(args, rank, world, dev):
         iteration()
     torch.cuda.synchronize(dev)
     steps = []
-    with Clocks(dev.index, enabled=not args.no_clocks and rank == 0) as clk:
+    with NvmlClocks(dev.index, enabled=not args.no_clocks and rank == 0) as clk:
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
