@@ -34,7 +34,8 @@ enum {
   TRNOPT_ERR_WORKSPACE = -3,        /* workspace missing or smaller than trnopt_workspace_size() */
   TRNOPT_ERR_UNSUPPORTED = -4,      /* shape or path not supported on this build / device */
   TRNOPT_ERR_CUDA = -5,             /* a CUDA runtime call failed (trnopt_last_cuda_error() has the code) */
-  TRNOPT_ERR_DEVICE = -6            /* a kernel reported an error flag (see trnopt_device_error_flags) */
+  TRNOPT_ERR_DEVICE = -6,           /* a kernel reported an error flag (see trnopt_device_error_flags) */
+  TRNOPT_ERR_TOO_LARGE = -7         /* needs more scratch than the library's static array (no-allocation entry) */
 };
 
 enum { TRNOPT_PATH_FFMA = 0, TRNOPT_PATH_TC = 1 };
@@ -92,6 +93,19 @@ int trnopt_pack_cloud(const float* xT, int ldx, int n, int d, int scale_exp, voi
 int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
                         const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
                         void* workspace, size_t ws_bytes, void* stream);
+
+/* The tensor-core half-step without a workspace argument, for callers that cannot allocate device memory (code
+ * inside someone else's stream capture, plugin hosts that only pass in/out buffers, arena allocators sized at
+ * start-up). No counterpart in the reference. Same arguments and results as trnopt_half_step_tc; the scratch is a
+ * static device array of trnopt_static_scratch_bytes() (4 MiB) per GPU, held until the process exits. Problems
+ * that need more (trnopt_workspace_size(rows, m, d, TRNOPT_PATH_TC) > 4 MiB) return TRNOPT_ERR_TOO_LARGE without
+ * launching. The first call on a GPU looks up the array's device address (cudaGetSymbolAddress) with that GPU
+ * current: make it before any stream capture. All calls on a GPU share the array: calls whose kernels overlap on
+ * the GPU (several streams or threads) race and give wrong results. Allocates nothing. */
+size_t trnopt_static_scratch_bytes(void);
+int trnopt_half_step_tc_static(const void* xpack, const float* xsq, const float* off, const void* ypack,
+                               const float* gh, const float* log_b, int rows, int m, int d, int sx, int sy, float eps,
+                               float kappa, float* fh, void* stream);
 
 /* Row log-sum-exp of a product, lse_i = log sum_j exp(xa_i . ya_j), xa_T (k, ldx), ya_T (k, ldy), 1 <= k <= 128.
  * Replaces make_row_lse_kernel(K, rows, m)(xa_T, ya_T) (nki_sinkhorn.py:150-172). */

@@ -83,6 +83,7 @@ const char* trnopt_status_string(int status) {
     case TRNOPT_ERR_UNSUPPORTED: return "unsupported shape or path";
     case TRNOPT_ERR_CUDA: return "CUDA runtime error";
     case TRNOPT_ERR_DEVICE: return "a kernel reported an error flag";
+    case TRNOPT_ERR_TOO_LARGE: return "problem needs more scratch than the static array of the no-allocation entry";
     default: return "unknown status";
   }
 }

@@ -46,6 +46,8 @@ _SIGS = {
     "trnopt_pack_bytes": (_Z, [_I, _I]),
     "trnopt_pack_cloud": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "trnopt_half_step_tc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _Z, _P]),
+    "trnopt_static_scratch_bytes": (_Z, []),
+    "trnopt_half_step_tc_static": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P]),
     "trnopt_median_workspace_size": (_Z, []),
     "trnopt_median_cost": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
 }
@@ -119,6 +121,13 @@ def half_step_tc(xpack, xsq, off, ypack, gh, log_b, rows, m, d, sx, sy, eps, kap
     check(lib.trnopt_half_step_tc(_ptr(xpack), _ptr(xsq), _ptr(off), _ptr(ypack), _ptr(gh), _ptr(log_b), rows, m, d,
                                   int(sx), int(sy), float(eps), float(kappa), _ptr(fh), _ptr(ws), ws.numel(),
                                   _stream()), "trnopt_half_step_tc")
+
+
+def half_step_tc_static(xpack, xsq, off, ypack, gh, log_b, rows, m, d, sx, sy, eps, kappa, fh) -> None:
+    """The tensor-core half-step with the library's static scratch instead of a workspace (allocates nothing)."""
+    check(lib.trnopt_half_step_tc_static(_ptr(xpack), _ptr(xsq), _ptr(off), _ptr(ypack), _ptr(gh), _ptr(log_b), rows,
+                                         m, d, int(sx), int(sy), float(eps), float(kappa), _ptr(fh), _stream()),
+          "trnopt_half_step_tc_static")
 
 
 def row_lse(xaT: torch.Tensor, yaT: torch.Tensor, ws: torch.Tensor | None = None) -> torch.Tensor:
