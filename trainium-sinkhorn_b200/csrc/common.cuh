@@ -23,6 +23,9 @@ constexpr double kLn2 = 0.6931471805599453;
 // Running-max floor: below every real score (padding scores are about -1.4e9 in base-2 units) and finite, so
 // 2^(t - M) never sees inf - inf. Columns past m get bias -inf and contribute exactly 0.
 constexpr float kMaxFloor = -1.0e30f;
+// Lazy max of the tensor-core epilogue: terms 2^(t - M) are allowed up to 2^kLazyMax before M is raised, so a row
+// sum stays below 2^(kLazyMax + 31) for any m < 2^31 (far from FP32 overflow) and rounding stays relative.
+constexpr float kLazyMax = 20.0f;
 
 // Device error word: bit flags set by kernels that give up a bounded wait. Read and cleared by the host API.
 enum ErrorBits : int {

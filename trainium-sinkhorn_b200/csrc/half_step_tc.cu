@@ -360,8 +360,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             t[j] = __uint_as_float(v[j]);
           }
           if (ch + 1 < TC_BN / 32) TRNOPT_TMEM_LD32(lane_addr + (uint32_t)((ch + 1) * 32), v);
+          // Lazy running max: the exps use the max known before this chunk (M), so they do not wait for this
+          // chunk's max, which is reduced alongside. Terms may exceed 1 by up to 2^kLazyMax; only a chunk whose
+          // max is above M + kLazyMax (the first chunk of a segment, and rare jumps) is redone with its own max.
           const float4* b4 = reinterpret_cast<const float4*>(bias + ch * 32);
-          float cmax = kMaxFloor;
+          float c0 = kMaxFloor, c1 = kMaxFloor, c2 = kMaxFloor, c3 = kMaxFloor;
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const float4 b = b4[q];
@@ -369,19 +373,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             t[4 * q + 1] = fmaf(t[4 * q + 1], dot2, b.y);
             t[4 * q + 2] = fmaf(t[4 * q + 2], dot2, b.z);
             t[4 * q + 3] = fmaf(t[4 * q + 3], dot2, b.w);
-            cmax = fmaxf(cmax, fmaxf(fmaxf(t[4 * q], t[4 * q + 1]), fmaxf(t[4 * q + 2], t[4 * q + 3])));
+            c0 = fmaxf(c0, t[4 * q + 0]);
+            c1 = fmaxf(c1, t[4 * q + 1]);
+            c2 = fmaxf(c2, t[4 * q + 2]);
+            c3 = fmaxf(c3, t[4 * q + 3]);
+            s0 += ex2_approx(t[4 * q + 0] - M);
+            s1 += ex2_approx(t[4 * q + 1] - M);
+            s2 += ex2_approx(t[4 * q + 2] - M);
+            s3 += ex2_approx(t[4 * q + 3] - M);
           }
-          if (cmax > M) {
-            L *= ex2_approx(M - cmax);
-            M = cmax;
-          }
-          float s0 = 0.f, s1 = 0.f;
+          const float cmax = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));
+          if (cmax > M + kLazyMax) {
+            const float Mn = cmax;
+            float r0 = 0.f, r1 = 0.f;
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            s0 += ex2_approx(t[j] - M);
-            s1 += ex2_approx(t[j + 1] - M);
+            for (int j = 0; j < 32; j += 2) {
+              r0 += ex2_approx(t[j] - Mn);
+              r1 += ex2_approx(t[j + 1] - Mn);
+            }
+            L = L * ex2_approx(M - Mn) + (r0 + r1);
+            M = Mn;
+          } else {
+            L += (s0 + s1) + (s2 + s3);
           }
-          L += s0 + s1;
           if (ch + 1 < TC_BN / 32) tmem_wait_ld();
         }
         tmem_fence_before();
