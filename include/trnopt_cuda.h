@@ -119,6 +119,10 @@ int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float*
                           float* out, void* stream);
 int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream);
 
+/* Self-test of the FMA-pipe 2^x used to balance exps between MUFU and the FMA units (no reference counterpart):
+ * out[i] = 2^x[i] for n floats, max relative error 2.1e-7 over [-125, 100]. */
+int trnopt_test_ex2_poly(const float* x, float* out, int n, void* stream);
+
 /* Exact median of all n m clamped costs max(C_ij, 0), C_ij = (sqx_i + sqy_j) - 2 xc_i . yc_j, float64, written to
  * out[0]; the mean of the two middle values when n m is even (np.median). xc (n, d) and yc (m, d) are row-major
  * centred points, sqx / sqy their squared norms. n m <= 1e8, d <= 128. Replaces the host NumPy median of

@@ -107,6 +107,19 @@ def test_half_step_matches_oracle(rows, m, d, eps, kappa, use_off, pad, path):
     assert np.all(np.isfinite(fh)) and err <= HS_TOL, err
 
 
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
+def test_padding_columns_before_real_ones(path):
+    """Zero-weight (log_b = -1e9) columns ahead of the real ones: the running max first settles on a padding score
+    near -1.4e9 and must recover full precision when the real columns arrive (any caller may order columns so)."""
+    rows, m, d, eps = 700, 3000, 30, 0.05
+    x, xsq, off, y, gh, lb = problem(rows, m, d, 5, eps)
+    lb[:700] = -1e9
+    fh = gpu_half_step(x, xsq, off, y, gh, lb, eps, 0.95, path=path)
+    ref = oracle_half_step(x, xsq, off, y, gh, lb, eps, 0.95)
+    err = np.abs(fh - ref).max() / eps
+    assert np.all(np.isfinite(fh)) and err <= HS_TOL, err
+
+
 def test_tc_and_ffma_agree_at_config_2_size():
     """One full-size config-2 half-step (10k x 10k, d 64, centred U[0,1] points) on both kernels."""
     from trnopt import synthetic
@@ -122,6 +135,18 @@ def test_tc_and_ffma_agree_at_config_2_size():
     assert np.abs(a[rows] - ref).max() / 0.1 <= HS_TOL
     assert np.abs(b[rows] - ref).max() / 0.1 <= HS_TOL
     assert np.abs(a - b).max() / 0.1 <= 2 * HS_TOL
+
+
+def test_fma_pipe_exp2_against_cuda_exp2f():
+    """The FMA-pipe 2^x (range reduction + degree-5 polynomial fitted for this library) against CUDA's exp2f
+    (torch.exp2 on the GPU) and against float64: relative error within 3e-7 over [-125, 100]."""
+    x = torch.cat([torch.linspace(-125, 100, 1_000_001), torch.linspace(-1, 1, 100_001)]).cuda()
+    got = _capi.test_ex2_poly(x)
+    ref_cuda = torch.exp2(x)
+    ref64 = torch.exp2(x.double())
+    assert ((got.double() / ref64 - 1).abs().max().item()) <= 3e-7
+    assert ((got / ref_cuda - 1).abs().max().item()) <= 5e-7
+    assert _capi.test_ex2_poly(torch.tensor([-1e9, -float("inf")], device="cuda")).max().item() < 1e-37
 
 
 def test_row_lse_reference_kat(golden):

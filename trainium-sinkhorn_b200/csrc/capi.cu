@@ -201,6 +201,11 @@ int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, c
   return cuda_status(tc_launch(p, xpack, ypack, sx, sy, sk, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int trnopt_test_ex2_poly(const float* x, float* out, int n, void* stream) {
+  if (!x || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  return cuda_status(ex2_poly_launch(x, out, n, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 size_t trnopt_median_workspace_size(void) { return median_workspace_bytes(); }
 
 int trnopt_median_cost(const double* xc, const double* yc, const double* sqx, const double* sqy, int n, int m, int d,

@@ -26,6 +26,8 @@ constexpr float kMaxFloor = -1.0e30f;
 // Lazy max of the tensor-core epilogue: terms 2^(t - M) are allowed up to 2^kLazyMax before M is raised, so a row
 // sum stays below 2^(kLazyMax + 31) for any m < 2^31 (far from FP32 overflow) and rounding stays relative.
 constexpr float kLazyMax = 20.0f;
+constexpr float kLazyRedo = 100.0f;      // a sum of 32 terms below 2^100 cannot have overflowed FP32
+constexpr float kLazyHeadroom = 8.0f;
 
 // Device error word: bit flags set by kernels that give up a bounded wait. Read and cleared by the host API.
 enum ErrorBits : int {

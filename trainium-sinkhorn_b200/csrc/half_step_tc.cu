@@ -10,12 +10,14 @@
 //
 // Per CTA (one per SM, persistent over a stream-K range of (128-row tile, 256-column tile) units):
 //   warp 8      TMA producer: row tiles (A, two buffers) and column tiles (B, a ring of stages) into 128B-swizzled
-//               shared memory; its lanes also write the tile's column bias (gh / eps + log b) * log2(e) to a ring.
+//               shared memory.
+//   warp 10     the tile's column bias (gh / eps + log b) * log2(e) into a 4-slot shared-memory ring.
 //   warp 9      allocates 512 TMEM columns and issues the MMAs (M 128, N 256, K 16; 3 dk / 16 per tile) into one
 //               of two 128 x 256 FP32 accumulators, committing to mbarriers.
-//   warps 0-7   two epilogue warpgroups, one per accumulator: each thread owns one row, reads its 256 scores of a
-//               tile from TMEM 32 at a time, adds the bias in FP32 and folds them into an online (max, sum) in
-//               base 2 (MUFU ex2). At the end of a segment each warpgroup writes its partial; the last arrival for
+//   warps 0-7   two epilogue warpgroups, each on half the columns of every tile: a thread owns one row, reads its
+//               128 scores of a tile from TMEM 64 at a time, adds the bias in FP32 and folds them into an online
+//               (max, sum) in base 2 (MUFU ex2, lazy max; see lse_tile128). The accumulator is released as soon
+//               as the tile's TMEM reads are done, before the last exps. At the end of a segment each warpgroup writes its partial; the last arrival for
 //               a row tile merges all partials and writes fh (common.cuh).
 // Every mbarrier wait is bounded (common.cuh kWaitLimitNs); a timeout sets the device error word and the CTA
 // unwinds (waits for its own copies and MMAs, frees TMEM) instead of hanging.
@@ -32,10 +34,12 @@ namespace trnopt {
 
 constexpr int TC_BM = 128;          // rows per tile (MMA M, TMEM lanes)
 constexpr int TC_BN = 256;          // columns per tile (MMA N)
-constexpr int TC_THREADS = 320;     // 8 epilogue warps + producer + MMA
-constexpr int TC_NBIAS = 4;         // bias ring slots
+constexpr int TC_NACC = 2;          // TMEM accumulators of TC_BN columns (512 columns in all)
+constexpr int TC_THREADS = 352;     // 8 epilogue warps + TMA producer + MMA + bias
+constexpr int TC_NBIAS = 8;         // bias ring slots
 constexpr int TC_PRODUCER_WARP = 8;
 constexpr int TC_MMA_WARP = 9;
+constexpr int TC_BIAS_WARP = 10;
 
 // ------------------------------------------------------------------------------------------------------------
 // PTX wrappers
@@ -109,16 +113,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-#define TRNOPT_TMEM_LD32(taddr, v)                                                                               \
-  asm volatile(                                                                                                  \
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, " \
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"              \
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),          \
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),    \
-        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),  \
-        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])   \
-      : "r"(taddr)                                                                                               \
-      : "memory")
+#define TRNOPT_TMEM_LD64(taddr, v) \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];" \
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63]) \
+               : "r"(taddr) : "memory")
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -134,7 +132,203 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: D F32, A and B FP16, both K-major, N = 256, M = 128.
+// Packed FP32 pair arithmetic (sm_100): two lanes of work per instruction on the FMA pipe.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// One block of 64 values of a row after the bias FMA, relative to `shift` (0 for a row's first block): the max and,
+// for a row past its first block, the lazy sum 2^(a_j) (exps relative to the running M = shift).
+template <int N>
+__device__ __forceinline__ void block_terms(uint32_t (&v)[N], const float* bh, uint64_t d2, float shift, float (&a)[N],
+                                            float& cmax) {
+  const uint64_t nm = pk2(-shift, -shift);
+  const float4* b4 = reinterpret_cast<const float4*>(bh);
+#pragma unroll
+  for (int q = 0; q < N / 4; ++q) {
+    const float4 b = b4[q];
+    const uint64_t u0 =
+        ffma2(pk2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])), d2, fadd2(pk2(b.x, b.y), nm));
+    const uint64_t u1 =
+        ffma2(pk2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])), d2, fadd2(pk2(b.z, b.w), nm));
+    upk2(u0, a[4 * q], a[4 * q + 1]);
+    upk2(u1, a[4 * q + 2], a[4 * q + 3]);
+  }
+  float c[4];                                                 // chain k reduces every fourth group of 8
+#pragma unroll
+  for (int k = 0; k < 4; ++k) c[k] = kMaxFloor;
+#pragma unroll
+  for (int g = 0; g < N / 8; ++g) {
+    const int b = 8 * g, k = g & 3;
+    c[k] = fmax3(c[k], a[b], a[b + 1]);
+    c[k] = fmax3(c[k], a[b + 2], a[b + 3]);
+    c[k] = fmax3(c[k], a[b + 4], a[b + 5]);
+    c[k] = fmax3(c[k], a[b + 6], a[b + 7]);
+  }
+  cmax = fmaxf(fmaxf(c[0], c[1]), fmaxf(c[2], c[3]));
+}
+
+// 2^x on the FMA pipe, to take a share of the exps off MUFU (16 results / clock / SM). Range reduction by the
+// round-to-integer add (x + 1.5 * 2^23 keeps round(x) in the low mantissa bits), 2^f on [-1/2, 1/2] by a degree-5
+// polynomial fitted for this library (relative minimax, Lawson-iterated least squares; fit error 7.5e-8), and the
+// integer part added to the exponent field. Max relative error 2.1e-7 over [-125, 100] (ex2.approx: ~2^-22).
+// Inputs below -125 are clamped (their terms are < 2^-125, nothing next to a row's largest term of >= 2^-8).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float y = x + 12582912.0f;
+  const float f = x - (y - 12582912.0f);
+  float p = 0x1.5c08dcp-10f;
+  p = fmaf(p, f, 0x1.3d0c54p-7f);
+  p = fmaf(p, f, 0x1.c6b6e6p-5f);
+  p = fmaf(p, f, 0x1.ebf918p-3f);
+  p = fmaf(p, f, 0x1.62e428p-1f);
+  p = fmaf(p, f, 0x1.000002p+0f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(y) << 23));
+}
+
+// sum_j 2^(a_j - off) on MUFU (ex2.approx), four independent packed partial sums.
+template <int N>
+__device__ __forceinline__ float exp_sum(const float (&a)[N], float off) {
+  uint64_t s0 = 0ull, s1 = 0ull, s2 = 0ull, s3 = 0ull;
+#pragma unroll
+  for (int j = 0; j < N; j += 8) {
+    s0 = fadd2(s0, pk2(ex2_approx(a[j] - off), ex2_approx(a[j + 1] - off)));
+    s1 = fadd2(s1, pk2(ex2_approx(a[j + 2] - off), ex2_approx(a[j + 3] - off)));
+    s2 = fadd2(s2, pk2(ex2_approx(a[j + 4] - off), ex2_approx(a[j + 5] - off)));
+    s3 = fadd2(s3, pk2(ex2_approx(a[j + 6] - off), ex2_approx(a[j + 7] - off)));
+  }
+  s0 = fadd2(s0, s1);
+  s2 = fadd2(s2, s3);
+  s0 = fadd2(s0, s2);
+  float x0, x1;
+  upk2(s0, x0, x1);
+  return x0 + x1;
+}
+
+// Redo of one block in absolute terms from the raw accumulators re-read from TMEM (into the registers of a[]).
+// The relative values lose their low bits when M is far below the block (e.g. M set by columns of PAD_LOG_WEIGHT,
+// -1e9). Warp-uniform entry (tcgen05.ld is .sync.aligned); only lanes with `redo` change (M, L).
+template <int N>
+__device__ __forceinline__ void block_redo(uint32_t taddr, const float* bh, float dot2, bool redo, float (&a)[N],
+                                           float& M, float& L) {
+  uint32_t* raw = reinterpret_cast<uint32_t*>(a);
+  TRNOPT_TMEM_LD64(taddr, raw);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < N; ++j) asm volatile("" : "+r"(raw[j]));
+  if (!redo) return;
+  const float4* b4 = reinterpret_cast<const float4*>(bh);
+  float tmax = kMaxFloor;
+#pragma unroll
+  for (int q = 0; q < N / 4; ++q) {
+    const float4 b = b4[q];
+    a[4 * q + 0] = fmaf(__uint_as_float(raw[4 * q + 0]), dot2, b.x);
+    a[4 * q + 1] = fmaf(__uint_as_float(raw[4 * q + 1]), dot2, b.y);
+    a[4 * q + 2] = fmaf(__uint_as_float(raw[4 * q + 2]), dot2, b.z);
+    a[4 * q + 3] = fmaf(__uint_as_float(raw[4 * q + 3]), dot2, b.w);
+    tmax = fmaxf(tmax, fmaxf(fmaxf(a[4 * q], a[4 * q + 1]), fmaxf(a[4 * q + 2], a[4 * q + 3])));
+  }
+  const float Mn = tmax + kLazyHeadroom;
+  L = L * ex2_approx(M - Mn) + exp_sum(a, Mn);
+  M = Mn;
+}
+
+// Lazy-max update of (M, L) with a block whose values a[] are relative to M (not a first block): the exps use the
+// max known before the block, so no exp waits for the block's max (reduced alongside). Terms may exceed 1 by up
+// to 2^kLazyMax; a block whose max is higher rescales its sum (no new exps) while no term can have overflowed
+// (max <= M + kLazyRedo); returns true when the block must be redone in absolute terms instead.
+template <int N>
+__device__ __forceinline__ bool block_fold(const float (&a)[N], float cmax, float& M, float& L) {
+  const float sum = exp_sum(a, 0.f);
+  if (cmax <= kLazyMax) {
+    L += sum;
+  } else if (cmax <= kLazyRedo) {
+    const float off = cmax + kLazyHeadroom;
+    L = (L + sum) * ex2_approx(-off);
+    M += off;
+  } else {
+    return true;
+  }
+  return false;
+}
+
+// First block of a row (M still at the floor): max first, then M = max + kLazyHeadroom.
+template <int N>
+__device__ __forceinline__ void block_first(const float (&a)[N], float cmax, float& M, float& L) {
+  if (!(cmax > kMaxFloor)) return;                            // only columns past m so far
+  M = cmax + kLazyHeadroom;
+  L = exp_sum(a, M);
+}
+
+// Fold one row's 128 accumulator values of a tile (TMEM address taddr, 32x32b lanes: this thread's row) into the
+// row's running base-2 (M, L):   t_j = acc_j * dot2 + bias_j,   L = sum_j 2^(t_j - M).
+// Two blocks of 64 values (u_j = t_j - M from one packed FMA, acc * dot2 + (bias - M)). Block 1 is loaded from TMEM
+// while block 0's exps run; once block 1 is loaded and its max (and any redo re-read) is done, every TMEM read of
+// the tile is over and the accumulator is released (tcgen05 fence, then an arrival on `acc_empty`) before block 1's
+// exps, so the MMAs two tiles ahead overlap them. Must be called by all 32 lanes of the warp.
+__device__ __forceinline__ void lse_tile128(uint32_t taddr, const float* bias, float dot2, float& M, float& L,
+                                            uint64_t* acc_empty) {
+  constexpr int N = 64;
+  const uint64_t d2 = pk2(dot2, dot2);
+  uint32_t v[N];
+  float a[N];
+  float cmax;
+  TRNOPT_TMEM_LD64(taddr, v);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < N; ++j) asm volatile("" : "+r"(v[j]));
+  // block 0
+  bool first = (M == kMaxFloor);
+  block_terms(v, bias, d2, first ? 0.f : M, a, cmax);
+  TRNOPT_TMEM_LD64(taddr + (uint32_t)N, v);                   // block 1 into the now-free registers
+  bool redo = false;
+  if (first) block_first(a, cmax, M, L);
+  else redo = block_fold(a, cmax, M, L);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < N; ++j) asm volatile("" : "+r"(v[j]));
+  if (__any_sync(0xffffffffu, redo)) block_redo(taddr, bias, dot2, redo, a, M, L);
+  // block 1: terms and max, then its redo re-read if any, then release the accumulator, then the exps
+  first = (M == kMaxFloor);
+  block_terms(v, bias + N, d2, first ? 0.f : M, a, cmax);
+  redo = !first && cmax > kLazyRedo;
+  if (__any_sync(0xffffffffu, redo)) {
+    // Rare: lanes without a redo fold block 1 first (a[] is then free), then the warp re-reads it for the others,
+    // then releases.
+    if (first) block_first(a, cmax, M, L);
+    else if (!redo) block_fold(a, cmax, M, L);
+    block_redo(taddr + (uint32_t)N, bias + N, dot2, redo, a, M, L);
+    tmem_fence_before();
+    mbar_arrive(acc_empty);
+  } else {
+    tmem_fence_before();
+    mbar_arrive(acc_empty);
+    if (first) block_first(a, cmax, M, L);
+    else block_fold(a, cmax, M, L);
+  }
+}
+
+// Instruction descriptor, kind::f16: D F32, A and B FP16, both K-major, N = TC_BN, M = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                             ((uint32_t)(TC_BM >> 4) << 24);
 
@@ -150,9 +344,9 @@ struct TcCfg {
   static constexpr int OFF_B = 2 * A_BYTES;
   static constexpr int OFF_BIAS = OFF_B + NS * B_BYTES;
   static constexpr int OFF_BAR = OFF_BIAS + TC_NBIAS * TC_BN * 4;
-  // barriers: full[NS], empty[NS], a_full[2], a_empty[2], acc_full[2], acc_empty[2], bias_full[NB], bias_empty[NB],
-  // drain[1]
-  static constexpr int NBAR = 2 * NS + 8 + 2 * TC_NBIAS + 1;
+  // barriers: full[NS], empty[NS], a_full[2], a_empty[2], acc_full[NACC], acc_empty[NACC], bias_full[NB],
+  // bias_empty[NB], drain[1]
+  static constexpr int NBAR = 2 * NS + 4 + 2 * TC_NACC + 2 * TC_NBIAS + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;     // + alignment slack for the 1024-byte aligned base
 };
@@ -180,8 +374,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* a_full = bars + 2 * C::NS;
   uint64_t* a_empty = a_full + 2;
   uint64_t* acc_full = a_empty + 2;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* bias_full = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + TC_NACC;
+  uint64_t* bias_full = acc_empty + TC_NACC;
   uint64_t* bias_empty = bias_full + TC_NBIAS;
   uint64_t* drain = bias_empty + TC_NBIAS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
@@ -195,11 +389,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NS; ++s) { mbar_init(&full_b[s], 1); mbar_init(&empty_b[s], 1); }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&a_full[b], 1); mbar_init(&a_empty[b], 1);
-      mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 128);
-    }
-    for (int s = 0; s < TC_NBIAS; ++s) { mbar_init(&bias_full[s], 32); mbar_init(&bias_empty[s], 128); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&a_full[b], 1); mbar_init(&a_empty[b], 1); }
+    for (int b = 0; b < TC_NACC; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 256); }
+    for (int s = 0; s < TC_NBIAS; ++s) { mbar_init(&bias_full[s], 32); mbar_init(&bias_empty[s], 256); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -253,19 +445,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tma_load_2d(smem + C::OFF_B + stage * C::B_BYTES + kb * TC_BN * 128, &map_b, &full_b[stage], kb * 64,
                         c * TC_BN);
         }
-        const int bslot = T % TC_NBIAS;
-        ok = mbar_wait(&bias_empty[bslot], ((T / TC_NBIAS) & 1) ^ 1, abort_flag, p.error_word);
-        if (!ok) break;
-        float* bias = bias_ring + bslot * TC_BN;
-#pragma unroll
-        for (int q = 0; q < TC_BN / 32; ++q) {
-          const int jj = q * 32 + lane;
-          const int j = c * TC_BN + jj;
-          float b = -INFINITY;
-          if (j < p.m) b = fmaf(p.log_b[j], p.lb2, p.gh[j] * p.gh2);
-          bias[jj] = b;
-        }
-        mbar_arrive(&bias_full[bslot]);
       }
     }
     // Unwind: make sure no copy of ours is still landing in shared memory when the CTA exits. Stage s has had
@@ -280,6 +459,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int fills = (seg_issued - a + 1) / 2;
         if (fills > 0) mbar_wait(&a_full[a], (uint32_t)((fills - 1) & 1), abort_flag, p.error_word, true);
       }
+    }
+  } else if (warp == TC_BIAS_WARP) {
+    // ---------------------------------------------------------------- column bias, (gh / eps + log b) log2(e)
+    // All loads of a tile are issued before any shared-memory store (restrict-qualified, read-only path), so a
+    // tile costs one L2 round trip; the 4-slot ring lets this warp run ahead of the epilogue.
+    const float* __restrict__ ghp = p.gh;
+    const float* __restrict__ lbp = p.log_b;
+    int T = 0;
+    bool ok = true;
+    for (long long u = u_begin; u < u_end && ok; ++u, ++T) {
+      const int c = (int)(u % sk.nct);
+      float g[TC_BN / 32], l[TC_BN / 32];
+#pragma unroll
+      for (int q = 0; q < TC_BN / 32; ++q) {
+        const int j = c * TC_BN + q * 32 + lane;
+        g[q] = j < p.m ? __ldg(ghp + j) : 0.f;
+        l[q] = j < p.m ? __ldg(lbp + j) : -INFINITY;
+      }
+      const int bslot = T % TC_NBIAS;
+      ok = mbar_wait(&bias_empty[bslot], ((T / TC_NBIAS) & 1) ^ 1, abort_flag, p.error_word);
+      if (!ok) break;
+      float* bias = bias_ring + bslot * TC_BN;
+#pragma unroll
+      for (int q = 0; q < TC_BN / 32; ++q) bias[q * 32 + lane] = fmaf(l[q], p.lb2, g[q] * p.gh2);
+      mbar_arrive(&bias_full[bslot]);
     }
   } else if (warp == TC_MMA_WARP) {
     // ---------------------------------------------------------------- MMA issuer
@@ -296,8 +500,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!ok) break;
         for (; u < seg_end; ++u, ++T) {
           const int stage = T % C::NS;
-          const int acc = T & 1;
-          ok = mbar_wait(&acc_empty[acc], ((T >> 1) & 1) ^ 1, abort_flag, p.error_word);
+          const int acc = T % TC_NACC;
+          ok = mbar_wait(&acc_empty[acc], ((T / TC_NACC) & 1) ^ 1, abort_flag, p.error_word);
           if (ok) ok = mbar_wait(&full_b[stage], (T / C::NS) & 1, abort_flag, p.error_word);
           if (!ok) break;
           tmem_fence_after();
@@ -330,9 +534,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- epilogue warpgroups 0 and 1
-    const int wg = warp >> 2;                  // which accumulator / which tiles (T % 2 == wg)
+    // Both warpgroups work on every tile: warpgroup wg takes columns [128 wg, 128 wg + 128) of the tile's
+    // accumulator and releases the accumulator as soon as its last TMEM read of the tile is done (inside
+    // lse_tile128), so the MMAs two tiles ahead overlap the rest of the fold.
+    const int wg = warp >> 2;
     const int qrow = (warp & 3) * 32 + lane;   // this thread's row in the tile == its TMEM lane
-    const uint32_t lane_addr = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(wg * TC_BN);
+    const uint32_t lane_base = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(wg * (TC_BN / 2));
     const float dot2 = p.dot2;
     int T = 0;
     bool ok = true;
@@ -341,65 +548,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
       float M = kMaxFloor, L = 0.f;
       for (; u < seg_end; ++u, ++T) {
-        if ((T & 1) != wg || !ok) continue;
-        ok = mbar_wait(&acc_full[wg], (T >> 1) & 1, abort_flag, p.error_word);
+        if (!ok) continue;
+        const int acc = T % TC_NACC;
+        ok = mbar_wait(&acc_full[acc], (T / TC_NACC) & 1, abort_flag, p.error_word);
         const int bslot = T % TC_NBIAS;
         if (ok) ok = mbar_wait(&bias_full[bslot], (T / TC_NBIAS) & 1, abort_flag, p.error_word);
         if (!ok) continue;
         tmem_fence_after();
-        const float* bias = bias_ring + bslot * TC_BN;
-        uint32_t v[32];
-        TRNOPT_TMEM_LD32(lane_addr, v);
-        tmem_wait_ld();
-#pragma unroll 1
-        for (int ch = 0; ch < TC_BN / 32; ++ch) {
-          float t[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            asm volatile("" : "+r"(v[j]));
-            t[j] = __uint_as_float(v[j]);
-          }
-          if (ch + 1 < TC_BN / 32) TRNOPT_TMEM_LD32(lane_addr + (uint32_t)((ch + 1) * 32), v);
-          // Lazy running max: the exps use the max known before this chunk (M), so they do not wait for this
-          // chunk's max, which is reduced alongside. Terms may exceed 1 by up to 2^kLazyMax; only a chunk whose
-          // max is above M + kLazyMax (the first chunk of a segment, and rare jumps) is redone with its own max.
-          const float4* b4 = reinterpret_cast<const float4*>(bias + ch * 32);
-          float c0 = kMaxFloor, c1 = kMaxFloor, c2 = kMaxFloor, c3 = kMaxFloor;
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 b = b4[q];
-            t[4 * q + 0] = fmaf(t[4 * q + 0], dot2, b.x);
-            t[4 * q + 1] = fmaf(t[4 * q + 1], dot2, b.y);
-            t[4 * q + 2] = fmaf(t[4 * q + 2], dot2, b.z);
-            t[4 * q + 3] = fmaf(t[4 * q + 3], dot2, b.w);
-            c0 = fmaxf(c0, t[4 * q + 0]);
-            c1 = fmaxf(c1, t[4 * q + 1]);
-            c2 = fmaxf(c2, t[4 * q + 2]);
-            c3 = fmaxf(c3, t[4 * q + 3]);
-            s0 += ex2_approx(t[4 * q + 0] - M);
-            s1 += ex2_approx(t[4 * q + 1] - M);
-            s2 += ex2_approx(t[4 * q + 2] - M);
-            s3 += ex2_approx(t[4 * q + 3] - M);
-          }
-          const float cmax = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));
-          if (cmax > M + kLazyMax) {
-            const float Mn = cmax;
-            float r0 = 0.f, r1 = 0.f;
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              r0 += ex2_approx(t[j] - Mn);
-              r1 += ex2_approx(t[j + 1] - Mn);
-            }
-            L = L * ex2_approx(M - Mn) + (r0 + r1);
-            M = Mn;
-          } else {
-            L += (s0 + s1) + (s2 + s3);
-          }
-          if (ch + 1 < TC_BN / 32) tmem_wait_ld();
-        }
-        tmem_fence_before();
-        mbar_arrive(&acc_empty[wg]);
+        lse_tile128(lane_base + (uint32_t)(acc * TC_BN), bias_ring + bslot * TC_BN + wg * (TC_BN / 2), dot2, M, L,
+                    &acc_empty[acc]);
         mbar_arrive(&bias_empty[bslot]);
       }
       // Segment done: this warpgroup's partial for row tile r, then one arrival on the row tile's counter.
@@ -453,6 +610,15 @@ __global__ void tc_pack_kernel(const float* __restrict__ xT, int ldx, int n, int
     }
     out[idx] = h;
   }
+}
+
+__global__ void ex2_poly_kernel(const float* __restrict__ x, float* __restrict__ out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = ex2_poly(x[i]);
+}
+
+cudaError_t ex2_poly_launch(const float* x, float* out, int n, cudaStream_t stream) {
+  ex2_poly_kernel<<<(n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184, 256, 0, stream>>>(x, out, n);
+  return cudaGetLastError();
 }
 
 int tc_dk(int d) { return (d + 15) / 16 * 16; }

@@ -35,6 +35,8 @@ size_t median_workspace_bytes();
 cudaError_t median_launch(const double* x, const double* y, const double* sqx, const double* sqy, int n, int m,
                           int d, double* out, void* ws, cudaStream_t stream);
 
+cudaError_t ex2_poly_launch(const float* x, float* out, int n, cudaStream_t stream);
+
 int* device_error_word();
 
 }  // namespace trnopt

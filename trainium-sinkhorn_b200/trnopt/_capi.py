@@ -48,6 +48,7 @@ _SIGS = {
     "trnopt_half_step_tc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _Z, _P]),
     "trnopt_static_scratch_bytes": (_Z, []),
     "trnopt_half_step_tc_static": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P]),
+    "trnopt_test_ex2_poly": (_I, [_P, _P, _I, _P]),
     "trnopt_median_workspace_size": (_Z, []),
     "trnopt_median_cost": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
 }
@@ -179,6 +180,14 @@ def median_cost(xc: torch.Tensor, yc: torch.Tensor, sqx: torch.Tensor, sqy: torc
     out = torch.empty(1, dtype=torch.float64, device=xc.device)
     check(lib.trnopt_median_cost(_ptr(xc), _ptr(yc), _ptr(sqx), _ptr(sqy), n, m, d, _ptr(out), _ptr(ws), ws.numel(),
                                  _stream()), "trnopt_median_cost")
+    return out
+
+
+def test_ex2_poly(x: torch.Tensor) -> torch.Tensor:
+    """2^x through the library's FMA-pipe exp2 (self-test hook)."""
+    _need(x, "x")
+    out = torch.empty_like(x)
+    check(lib.trnopt_test_ex2_poly(_ptr(x), _ptr(out), x.numel(), _stream()), "trnopt_test_ex2_poly")
     return out
 
 
