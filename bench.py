@@ -7,6 +7,9 @@ Workloads (synthetic, seeded; trnopt.synthetic):
   weak  the N > 1 default: n = 10,000 N rows, m = 10,000, d = 64 (config 2's per-GPU work at every N)
   cfg5  n = m = 262,144, d = 64, x, y ~ N(0, I)/8, mean-normalised cost, eps 0.01 (strong
         scaling over N)
+  cfg3  one wot transport map, 7,355 x 8,962 cells in d = 30 (median cost, eps 0.05, lambda (1, 50), 3 growth
+        iterations, tol 1e-8): a step is the whole map through the public API, reported in seconds
+  cfg4  the 38-pair trajectory pipeline (175k cells) with cfg3's settings: a step is the whole pipeline, seconds
 A step is one Sinkhorn iteration with the inputs resident in HBM; L2 (126 MB) is flushed between timed steps by
 writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU, rows of every
 half-step are split across the ranks and the new potential is all-gathered with NCCL; the reported time is the
@@ -45,7 +48,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4"])
     ap.add_argument("--path", default="auto", choices=["auto", "ffma", "tc"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -62,7 +65,7 @@ def workload(name: str, world: int):
         x, y = synthetic.cfg2()
         return name, x, y, dict(eps=0.1, normalize=False), {"n": 10_000, "m": 10_000, "d": 64, "eps": 0.1}
     if name == "weak":
-        x, y = synthetic.cfg2(n=10_000 * world)
+        x, y = synthetic.cfg2(n=10_000 * world, m=10_000)
         return name, x, y, dict(eps=0.1, normalize=False), {"n": 10_000 * world, "m": 10_000, "d": 64, "eps": 0.1}
     x, y = synthetic.cfg5()
     return name, x, y, dict(eps=0.01, normalize="mean"), {"n": len(x), "m": len(y), "d": 64, "eps": 0.01}
@@ -260,6 +263,49 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_pipeline(args, rank, world, dev):
+    """cfg3 / cfg4: wot transport maps through the public API (trnopt.singlecell), wall time per map / pipeline."""
+    from trnopt import Backend, SinkhornOptions, synthetic
+    from trnopt.singlecell import wot_transport_map
+    opts = SinkhornOptions(backend=Backend.preset("cuda-fused", device=str(dev)), cores=world)
+    if args.workload == "cfg3":
+        x0, x1, g = synthetic.cfg3()
+        pairs = [(x0, x1, g)]
+        cfg = {"workload": "cfg3", "n": len(x0), "m": len(x1), "d": 30, "eps": 0.05, "lambda": [1.0, 50.0],
+               "growth_iters": 3, "tol": 1e-8}
+    else:
+        tr = synthetic.cfg4()
+        pairs = [(tr.cohorts[t], tr.cohorts[t + 1], tr.growth[t]) for t in range(len(tr.cohorts) - 1)]
+        cfg = {"workload": "cfg4", "pairs": len(pairs), "cells": int(sum(len(c) for c in tr.cohorts)), "d": 30,
+               "eps": 0.05, "lambda": [1.0, 50.0], "growth_iters": 3, "tol": 1e-8}
+
+    def one():
+        iters = 0
+        for x0, x1, g in pairs:
+            tm = wot_transport_map(x0, x1, g, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8, opts=opts)
+            iters += tm.iterations
+        return iters
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize(dev)
+    times, iters = [], 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        iters = one()
+        torch.cuda.synchronize(dev)
+        times.append(time.perf_counter() - t0)
+    v = float(np.mean(times))
+    if rank == 0:
+        line = {"metric": "wot transport map seconds" if args.workload == "cfg3" else "38-pair pipeline seconds",
+                "value": v, "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded generators in trnopt.synthetic)",
+                "config": {**cfg, "sinkhorn_iterations": iters, "ms_per_iteration": v * 1e3 / max(1, iters)},
+                "gpu_launches": 2 * iters}
+        print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank, world, dev):
     import trnopt.sinkhorn  # noqa: F401
     from trnopt import Backend, SinkhornOptions, _capi, sinkhorn
@@ -406,7 +452,10 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     try:
-        run_ours(args, rank, world, dev)
+        if args.workload in ("cfg3", "cfg4"):
+            run_pipeline(args, rank, world, dev)
+        else:
+            run_ours(args, rank, world, dev)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

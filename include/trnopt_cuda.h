@@ -119,6 +119,19 @@ int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float*
                           float* out, void* stream);
 int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream);
 
+/* n_iter Sinkhorn iterations in one call: for i < n_iter, with g = (start_parity + i) odd ? g1 : g0 and the other
+ * buffer g',  fh <- half_step(x side, y side, g, kappa_x);  g' <- half_step(y side, x side, fh, kappa_y),
+ * i.e. the body of the reference's loop, sweep(Xs, Ys, ...) then sweep(Ys, Xs, ...) (sinkhorn.py:353-354),
+ * queued from C so a run of iterations between host checks costs one call. path TRNOPT_PATH_TC takes packed clouds
+ * (x_op, y_op from trnopt_pack_cloud, scales sx, sy; ldx, ldy unused); TRNOPT_PATH_FFMA takes transposed clouds
+ * (x_op = xT (d, ldx), y_op = yT (d, ldy)). nx, ny are the (padded) point counts, log_a / log_b the log weights,
+ * xoff / yoff the row offsets (or NULL). One workspace sized for the larger of the two half-steps. */
+int trnopt_sinkhorn_run(int path, const void* x_op, int ldx, const float* xsq, const float* xoff, const float* log_a,
+                        int nx, int sx, const void* y_op, int ldy, const float* ysq, const float* yoff,
+                        const float* log_b, int ny, int sy, int d, float* g0, float* g1, float* fh, int start_parity,
+                        int n_iter, float eps, float kappa_x, float kappa_y, void* workspace, size_t ws_bytes,
+                        void* stream);
+
 /* Self-test of the FMA-pipe 2^x used to balance exps between MUFU and the FMA units (no reference counterpart):
  * out[i] = 2^x[i] for n floats, max relative error 2.1e-7 over [-125, 100]. */
 int trnopt_test_ex2_poly(const float* x, float* out, int n, void* stream);

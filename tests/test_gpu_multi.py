@@ -1,0 +1,38 @@
+"""Rows of every half-step split across 2 GPUs (one process per GPU, NCCL all-gather of the new potential) give the
+single-GPU answer: the counterpart of the reference's two-cores-match-one test (tests/test_sinkhorn.py:174-183)."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpus_match_one(tmp_path):
+    from trnopt import Backend, SinkhornOptions, sinkhorn
+    out = tmp_path / "two.npz"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29600 + os.getpid() % 200}",
+           str(ROOT / "tests" / "dist_solver_worker.py"), str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    z = np.load(out)
+    rng = np.random.default_rng(0)
+    x, y = rng.uniform(size=(1500, 16)), rng.uniform(size=(1300, 16))
+    be = Backend.preset("cuda-fused")
+    one = sinkhorn(x, y, opts=SinkhornOptions(eps=0.1, max_iters=60, fixed_iters=True, normalize=False, backend=be))
+    np.testing.assert_allclose(z["f"], one.f, atol=1e-5 * 0.1)
+    np.testing.assert_allclose(z["g"], one.g, atol=1e-5 * 0.1)
+    xu, yu = rng.uniform(size=(700, 8)), rng.uniform(size=(650, 8))
+    a = rng.uniform(0.5, 1.5, 700) / 700
+    ru = sinkhorn(xu, yu, a=a, opts=SinkhornOptions(eps=0.1, rho=1.0, tol=1e-5, max_iters=3000, backend=be))
+    assert int(z["iters"]) == ru.iterations
+    np.testing.assert_allclose(z["fu"], ru.f, atol=1e-5)
+    np.testing.assert_allclose(z["row_mass"], ru.row_mass, rtol=1e-4)

@@ -10,10 +10,30 @@
 namespace trnopt {
 
 __device__ int g_error_word;
+
+// Per-device lookups cached once per device (the launch path queries them on every half-step).
+namespace {
+constexpr int kMaxDev = 64;
+int* g_error_ptr[kMaxDev] = {};
+int g_cc_major[kMaxDev] = {};
+}  // namespace
+
 int* device_error_word() {
-  int* p = nullptr;
-  cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word);
-  return p;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDev) dev = 0;
+  if (g_error_ptr[dev] == nullptr) {
+    int* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word) == cudaSuccess) g_error_ptr[dev] = p;
+    return p;
+  }
+  return g_error_ptr[dev];
+}
+
+int device_cc_major(int dev) {
+  if (dev < 0 || dev >= kMaxDev) return 0;
+  if (g_cc_major[dev] == 0) cudaDeviceGetAttribute(&g_cc_major[dev], cudaDevAttrComputeCapabilityMajor, dev);
+  return g_cc_major[dev];
 }
 
 }  // namespace trnopt
@@ -183,9 +203,7 @@ int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, c
   if (!aligned(xpack, 128) || !aligned(ypack, 128)) return TRNOPT_ERR_ALIGNMENT;
   if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
   const int dev = current_device();
-  int major = 0;
-  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-  if (major != 10) return TRNOPT_ERR_UNSUPPORTED;
+  if (device_cc_major(dev) != 10) return TRNOPT_ERR_UNSUPPORTED;
   LseProblem p{};
   p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off; p.rows = rows; p.m = m; p.d = d;
   const double inv_eps = 1.0 / (double)eps;
@@ -204,6 +222,38 @@ int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, c
 int trnopt_test_ex2_poly(const float* x, float* out, int n, void* stream) {
   if (!x || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
   return cuda_status(ex2_poly_launch(x, out, n, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_sinkhorn_run(int path, const void* x_op, int ldx, const float* xsq, const float* xoff, const float* log_a,
+                        int nx, int sx, const void* y_op, int ldy, const float* ysq, const float* yoff,
+                        const float* log_b, int ny, int sy, int d, float* g0, float* g1, float* fh, int start_parity,
+                        int n_iter, float eps, float kappa_x, float kappa_y, void* workspace, size_t ws_bytes,
+                        void* stream) {
+  if (n_iter < 0 || !g0 || !g1 || !fh) return TRNOPT_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < n_iter; ++i) {
+    float* gc = ((start_parity + i) & 1) ? g1 : g0;
+    float* gn = ((start_parity + i) & 1) ? g0 : g1;
+    int st;
+    if (path == TRNOPT_PATH_TC) {
+      st = trnopt_half_step_tc(x_op, xsq, xoff, y_op, gc, log_b, nx, ny, d, sx, sy, eps, kappa_x, fh, workspace,
+                               ws_bytes, stream);
+      if (st == TRNOPT_OK)
+        st = trnopt_half_step_tc(y_op, ysq, yoff, x_op, fh, log_a, ny, nx, d, sy, sx, eps, kappa_y, gn, workspace,
+                                 ws_bytes, stream);
+    } else if (path == TRNOPT_PATH_FFMA) {
+      const float* xT = static_cast<const float*>(x_op);
+      const float* yT = static_cast<const float*>(y_op);
+      st = trnopt_half_step(xT, ldx, xsq, xoff, yT, ldy, gc, log_b, nx, ny, d, eps, kappa_x, fh, workspace, ws_bytes,
+                            stream);
+      if (st == TRNOPT_OK)
+        st = trnopt_half_step(yT, ldy, ysq, yoff, xT, ldx, fh, log_a, ny, nx, d, eps, kappa_y, gn, workspace,
+                              ws_bytes, stream);
+    } else {
+      st = TRNOPT_ERR_INVALID_ARGUMENT;
+    }
+    if (st != TRNOPT_OK) return st;
+  }
+  return TRNOPT_OK;
 }
 
 size_t trnopt_median_workspace_size(void) { return median_workspace_bytes(); }

@@ -410,6 +410,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the next half-step may start its prologue, TMA loads and MMAs (which read only
+  // the packed clouds) on SMs this grid has left; its bias warp waits for this grid's completion before reading
+  // the potential this grid writes, and everything it writes waits on that bias.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const long long u_begin = sk_unit_begin(blockIdx.x, sk.units, sk.grid);
   const long long u_end = sk_unit_begin(blockIdx.x + 1, sk.units, sk.grid);
@@ -466,6 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // tile costs one L2 round trip; the 4-slot ring lets this warp run ahead of the epilogue.
     const float* __restrict__ ghp = p.gh;
     const float* __restrict__ lbp = p.log_b;
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // the previous grid (which may write gh) is complete
     int T = 0;
     bool ok = true;
     for (long long u = u_begin; u < u_end && ok; ++u, ++T) {
@@ -723,8 +728,17 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  half_step_tc_kernel<NKB><<<a.sk.grid, TC_THREADS, C::SMEM, stream>>>(ma, mb, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.sk.grid);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, half_step_tc_kernel<NKB>, ma, mb, a);
 }
 
 cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,

@@ -49,6 +49,8 @@ _SIGS = {
     "trnopt_static_scratch_bytes": (_Z, []),
     "trnopt_half_step_tc_static": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P]),
     "trnopt_test_ex2_poly": (_I, [_P, _P, _I, _P]),
+    "trnopt_sinkhorn_run": (_I, [_I, _P, _I, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I,
+                                 _F, _F, _F, _P, _Z, _P]),
     "trnopt_median_workspace_size": (_Z, []),
     "trnopt_median_cost": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
 }
@@ -189,6 +191,15 @@ def test_ex2_poly(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(x)
     check(lib.trnopt_test_ex2_poly(_ptr(x), _ptr(out), x.numel(), _stream()), "trnopt_test_ex2_poly")
     return out
+
+
+def sinkhorn_run(path, x_op, ldx, xsq, xoff, log_a, nx, sx, y_op, ldy, ysq, yoff, log_b, ny, sy, d, g0, g1, fh,
+                 start_parity, n_iter, eps, kappa_x, kappa_y, ws) -> None:
+    """Queue n_iter iterations (f then g half-step each) with ping-pong g buffers g0 / g1 in one C call."""
+    check(lib.trnopt_sinkhorn_run(path, _ptr(x_op), ldx, _ptr(xsq), _ptr(xoff), _ptr(log_a), nx, int(sx), _ptr(y_op),
+                                  ldy, _ptr(ysq), _ptr(yoff), _ptr(log_b), ny, int(sy), d, _ptr(g0), _ptr(g1),
+                                  _ptr(fh), int(start_parity), int(n_iter), float(eps), float(kappa_x),
+                                  float(kappa_y), _ptr(ws), ws.numel(), _stream()), "trnopt_sinkhorn_run")
 
 
 def device_error_flags() -> int:

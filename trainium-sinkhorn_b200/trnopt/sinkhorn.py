@@ -154,24 +154,29 @@ class _Cloud:
         n, d = pts.shape
         unit = ROW_TILE * shards
         npad = -(-n // unit) * unit
-        P = np.zeros((npad, d))
-        P[:n] = pts
-        L = np.full(npad, PAD_LOG_WEIGHT)
-        L[:n] = log_w
-        O = np.zeros(npad)
-        if off is not None:
-            O[:n] = off
-        f32 = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32).to(dev)
         self.n, self.npad, self.d, self.shards = n, npad, d, shards
-        self.xT = f32(P.T)
-        self.sq64 = (P * P).sum(axis=1)
-        self.sq = f32(self.sq64)
-        self.log_w = f32(L)
-        self.w = f32(np.exp(L))
-        self.off = f32(O)
+        # Points go up once as (n, d) float32; padding and the transpose happen on the device.
+        p32 = torch.from_numpy(np.ascontiguousarray(pts, dtype=np.float32))
+        if dev.type == "cuda":
+            p32 = p32.pin_memory()
+        xT = torch.zeros((d, npad), dtype=torch.float32, device=dev)
+        xT[:, :n] = p32.to(dev, non_blocking=True).T
+        self.xT = xT
+        sq = np.zeros(npad)
+        sq[:n] = (pts * pts).sum(axis=1)                   # float64 on the host, then cast (sinkhorn.py:149)
+        self.sq64 = sq
+        vec = np.zeros((4, npad))
+        vec[0] = sq
+        vec[1] = PAD_LOG_WEIGHT
+        vec[1, :n] = log_w
+        vec[2] = np.exp(vec[1])
+        if off is not None:
+            vec[3, :n] = off
+        v32 = torch.from_numpy(vec.astype(np.float32)).to(dev)
+        self.sq, self.log_w, self.w, self.off = v32[0], v32[1], v32[2], v32[3]
         self.zero = torch.zeros(npad, dtype=torch.float32, device=dev)
-        self.h2d_bytes = 4 * (P.size + 4 * npad)
-        self.sexp = _scale_exp(P)
+        self.h2d_bytes = 4 * (n * d + 4 * npad)
+        self.sexp = _scale_exp(pts)
         self.packed = None
 
     def pack(self) -> None:
@@ -231,6 +236,30 @@ class _Off:
 
     def data_ptr(self) -> int:
         return self.t.data_ptr() + self.itemsize * self.offset
+
+
+class _Runs:
+    """Runs of n iterations (f then g half-step each) at one (eps, kappa_x, kappa_y). On one GPU a run is queued by a
+    single C call (trnopt_sinkhorn_run: the loop body of sinkhorn.py:353-354 issued from C), so the host costs one
+    call per run between checks instead of two per iteration. With row shards the run goes half-step by half-step,
+    each followed by its NCCL all-gather."""
+
+    def __init__(self, step, X, Y, G, fh, use_off: bool = True):
+        self.step, self.X, self.Y, self.G, self.fh = step, X, Y, G, fh
+        self.fused = step.shards == 1
+
+    def run(self, it, n, e, kx, ky):
+        X, Y, G, fh, st = self.X, self.Y, self.G, self.fh, self.step
+        if not self.fused:
+            for i in range(it, it + n):
+                st(X, Y, G[i % 2], e, kx, out=fh)
+                st(Y, X, fh, e, ky, out=G[(i + 1) % 2])
+            return
+        tc = st.path == "tc"
+        _capi.sinkhorn_run(_capi.PATH_TC if tc else _capi.PATH_FFMA,
+                           X.packed if tc else X.xT, X.npad, X.sq, X.off, X.log_w, X.npad, X.sexp,
+                           Y.packed if tc else Y.xT, Y.npad, Y.sq, Y.off, Y.log_w, Y.npad, Y.sexp, X.d,
+                           G[0], G[1], fh, it % 2, n, e, kx, ky, st.ws)
 
 
 def _prepare_path(path: str, X: _Cloud, Y: _Cloud) -> None:
@@ -316,10 +345,11 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         # gh = |ys|^2 - |yi|^2 (exactly the same iteration).
         gh0 = np.zeros(Y.npad)
         gh0[:Y.n] = (ys * ys).sum(1) - (yi * yi).sum(1)
-        gh = torch.as_tensor(gh0, dtype=torch.float32).to(dev)
+        # Ping-pong potentials: before iteration i the shifted g is G[i % 2]; fh has one buffer.
+        G = [torch.as_tensor(gh0, dtype=torch.float32).to(dev), torch.empty(Y.npad, dtype=torch.float32, device=dev)]
         fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
-        bufs = [torch.empty(Y.npad, dtype=torch.float32, device=dev) for _ in range(2)]
         err_dev = torch.zeros(1, dtype=torch.float32, device=dev)
+        runner = _Runs(step, X, Y, G, fh)
         err, converged, it = float("nan"), False, 0
         stage, stage_it = 0, 0
         stage_tol = max(opts.stage_tol, 1e-5)              # float32 floors (sinkhorn.py:342-344)
@@ -327,36 +357,41 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         while it < opts.max_iters:
+            # The loop of sinkhorn.py:346-378, advanced a run of iterations at a time: a run ends where the host
+            # has to look (a check, an eps change, max_iters), so the iterations inside it are one C call.
             if stages:
                 e = stages[stage] if stage < len(stages) else opts.eps
             else:
                 e = sched[it] if it < len(sched) else opts.eps
+            if not stages and it < len(sched):
+                n = 1                                          # eps-scaling schedule: eps changes every iteration
+            else:
+                n = opts.check_every - (stage_it % opts.check_every)
+            n = min(n, opts.max_iters - it)
+            runner.run(it, n, e, kap(e, rho_x), kap(e, rho_y))
+            it += n
+            stage_it += n
+            gh_prev, gh_new = G[(it - 1) % 2], G[it % 2]
             inv_eps = float(np.float32(1.0 / e))
-            step(X, Y, gh, e, kap(e, rho_x), out=fh)
-            gh_new = bufs[it % 2] if bufs[it % 2] is not gh else bufs[(it + 1) % 2]
-            step(Y, X, fh, e, kap(e, rho_y), out=gh_new)
-            it += 1
-            stage_it += 1
             if stages and stage < len(stages):
                 if stage_it % opts.check_every == 0:
-                    _capi.max_change(gh, gh_new, Y.n, inv_eps, err_dev)
+                    _capi.max_change(gh_prev, gh_new, Y.n, inv_eps, err_dev)
                     ch = float(err_dev.item())
                     if ch < stage_tol or stage_it >= opts.stage_max_iters:
                         stage, stage_it = stage + 1, 0
-                gh = gh_new
                 continue
             check = (not opts.fixed_iters and (stages or it > len(sched))
                      and (stage_it % opts.check_every == 0 or it == opts.max_iters))
             if check:
                 if balanced:
-                    _capi.balanced_error(gh, gh_new, Y.w, Y.npad, inv_eps, err_dev)
+                    _capi.balanced_error(gh_prev, gh_new, Y.w, Y.npad, inv_eps, err_dev)
                 else:
-                    _capi.max_change(gh, gh_new, Y.n, inv_eps, err_dev)
+                    _capi.max_change(gh_prev, gh_new, Y.n, inv_eps, err_dev)
                 err = float(err_dev.item())
-            gh = gh_new
             if check and err < tol:
                 converged = True
                 break
+        gh = G[it % 2]
         f = fh[:X.n].to(torch.float64).cpu().numpy() + X.sq64[:X.n]
         g = gh[:Y.n].to(torch.float64).cpu().numpy() + Y.sq64[:Y.n]
         row_mass = col_mass = None
