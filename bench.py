@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4"])
     ap.add_argument("--path", default="auto", choices=["auto", "ffma", "tc"])
+    ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
+                    help="N > 1: peer stores from the half-step kernels (tc path) or an NCCL all-gather per half-step")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
@@ -327,20 +329,42 @@ def run_ours(args, rank, world, dev):
     S._prepare_path(path, X, Y)
     ws = S._workspace(X, Y, world, dev, path)
     step = S._CudaStep(dev, world, rank, ws, path=path)
-    gh = torch.zeros(Y.npad, dtype=torch.float32, device=dev)
-    fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
+    exchange = S._exchange(args.exchange, path) if world > 1 else "none"
+    peer = None
+    if exchange == "peer":
+        from trnopt import _comm
+        peer = _comm.region(4 * (X.npad + 2 * Y.npad))
+        fh = peer.tensor(0, X.npad)
+        G = [peer.tensor(4 * X.npad, Y.npad), peer.tensor(4 * (X.npad + Y.npad), Y.npad)]
+        G[0].zero_()
+        fh.zero_()
+        peer.arrive()
+    else:
+        G = [torch.zeros(Y.npad, dtype=torch.float32, device=dev) for _ in range(2)]
+        fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
+    tc = path == "tc"
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
+    counter = [0]
 
     def iteration(ev=None):
+        # one iteration = f half-step then g half-step, through the same run entries the solver uses
+        i = counter[0]
+        counter[0] += 1
         if ev is not None:
             ev[0].record(stream)
-        step(X, Y, gh, eps, 1.0, out=fh)
+        if peer is not None:
+            _capi.sinkhorn_run_sharded(peer.comm, X.packed, X.sq, None, X.log_w, X.npad, X.sexp, Y.packed, Y.sq, None,
+                                       Y.log_w, Y.npad, Y.sexp, X.d, G[0], G[1], fh, i % 2, 1, eps, 1.0, 1.0, ws)
+        elif world > 1:
+            step(X, Y, G[i % 2], eps, 1.0, out=fh)
+            step(Y, X, fh, eps, 1.0, out=G[(i + 1) % 2])
+        else:
+            _capi.sinkhorn_run(_capi.PATH_TC if tc else _capi.PATH_FFMA, X.packed if tc else X.xT, X.npad, X.sq, None,
+                               X.log_w, X.npad, X.sexp, Y.packed if tc else Y.xT, Y.npad, Y.sq, None, Y.log_w, Y.npad,
+                               Y.sexp, X.d, G[0], G[1], fh, i % 2, 1, eps, 1.0, 1.0, ws)
         if ev is not None:
             ev[1].record(stream)
-        step(Y, X, fh, eps, 1.0, out=gh)
-        if ev is not None:
-            ev[2].record(stream)
 
     for _ in range(args.warmup):
         iteration()
@@ -353,15 +377,15 @@ def run_ours(args, rank, world, dev):
         for _ in range(args.steps):
             if not args.no_flush:
                 flush.zero_()
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
             iteration(ev)
             steps.append(ev)
         torch.cuda.synchronize(dev)
         if world > 1:
             torch.distributed.barrier()
-    step_ms = [a.elapsed_time(c) for a, _, c in steps]
-    f_ms = [a.elapsed_time(b) for a, b, _ in steps]
-    g_ms = [b.elapsed_time(c) for _, b, c in steps]
+    if peer is not None:
+        peer.wait()
+    step_ms = [a.elapsed_time(b) for a, b in steps]
     total = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(total, op=torch.distributed.ReduceOp.MAX)
@@ -370,9 +394,10 @@ def run_ours(args, rank, world, dev):
     if _capi.device_error_flags():
         raise RuntimeError("a kernel reported device error flags during the timed region")
 
-    # Roofline of the dominant kernel (the fused half-step): per launch, useful FLOPs 2 rows m d, exps rows m.
+    # Roofline of the dominant kernel (the fused half-step): per launch, useful FLOPs 2 rows m d, exps rows m. A step
+    # is two launches of it (f then g, the second allowed to start its prologue early), so a launch is half a step.
     rows_f, rows_g = X.npad // world, Y.npad // world
-    launch_ms = (statistics.mean(f_ms) + statistics.mean(g_ms)) / 2
+    launch_ms = statistics.mean(step_ms) / 2
     flops = (2.0 * rows_f * Y.npad * X.d + 2.0 * rows_g * X.npad * X.d) / 2
     exps = (rows_f * Y.npad + rows_g * X.npad) / 2.0
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
@@ -399,9 +424,9 @@ def run_ours(args, rank, world, dev):
     e2e = None
     if not args.no_e2e:
         opts = SinkhornOptions(max_iters=args.steps, fixed_iters=True, backend=Backend.preset("cuda-fused", device=str(dev)),
-                               cores=world, cuda_path=path, **kw)
+                               cores=world, cuda_path=path, cuda_exchange=args.exchange, **kw)
         sinkhorn(x[:256], y[:256], opts=SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend,
-                                                         cores=world, cuda_path=path, **kw))
+                                                         cores=world, cuda_path=path, cuda_exchange=args.exchange, **kw))
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
@@ -429,7 +454,7 @@ def run_ours(args, rank, world, dev):
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": False,
                 "scaling": "strong" if name in ("cfg2", "cfg5") else "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded generators in trnopt.synthetic)",
-                "config": {"workload": name, **cfg, "path": path, "shards": world,
+                "config": {"workload": name, **cfg, "path": path, "shards": world, "exchange": exchange,
                            "l2": "flushed between timed steps (256 MB write)"},
                 "gpu_launches": 2 * args.steps, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks}
         print(json.dumps(line), flush=True)

@@ -145,6 +145,67 @@ size_t trnopt_median_workspace_size(void);
 int trnopt_median_cost(const double* xc, const double* yc, const double* sqx, const double* sqy, int n, int m, int d,
                        double* out, void* workspace, size_t ws_bytes, void* stream);
 
+/* Multi-GPU (one process per GPU, up to 8): a peer-mapped region per rank and a sharded run that publishes each
+ * half-step's rows straight into every GPU's copy of the potential over NVLink. Replaces the reference's
+ * cross-core exchange after each half-step (sinkhorn.py:295-311: blocks split over cores, then concatenated on
+ * the host) and the all-gather a per-half-step design would need.
+ *
+ *   trnopt_comm_create    allocate this rank's region (bytes for the caller's buffers, after a 256-byte flag
+ *                         header) on the current device and write its IPC handle (trnopt_comm_handle_bytes bytes)
+ *                         to handle_out. Blocking.
+ *   trnopt_comm_open      map every other rank's region from the world handles (rank order, concatenated), which
+ *                         the caller exchanges through its process group. Blocking.
+ *   trnopt_comm_buffer    this rank's buffers (the same offset names the same vector on every rank).
+ *   trnopt_comm_arrive    queue a signal to every rank that this rank's stream has reached this point (call it
+ *                         after initialising the buffers of a solve, before its first run).
+ *   trnopt_comm_wait      queue a wait until every other rank has published everything this rank has published
+ *                         so far; call before reading a gathered vector outside the run (checks, downloads).
+ *   trnopt_sinkhorn_run_sharded
+ *                         trnopt_sinkhorn_run (TRNOPT_PATH_TC) over row shards: rank r computes rows
+ *                         [r nx / W, (r + 1) nx / W) of each f half-step and the same share of each g half-step
+ *                         and publishes them; g0, g1 and fh must lie in the comm buffer; nx, ny multiples of 128 W.
+ *   trnopt_comm_destroy   unmap the peers and free the region. Every rank must be past its last access to the
+ *                         others' regions (synchronise, then a host barrier) before any rank destroys.
+ * Every rank makes the same sequence of arrive / run / wait calls. All waits are bounded (4 s): an expired wait
+ * sets error flag 8 (trnopt_device_error_flags). Epochs, not the calls, order the GPUs: no host synchronisation
+ * is needed between runs. */
+size_t trnopt_comm_handle_bytes(void);
+int trnopt_comm_create(int rank, int world, size_t bytes, void** comm_out, void* handle_out);
+int trnopt_comm_open(void* comm, const void* handles);
+void* trnopt_comm_buffer(void* comm);
+size_t trnopt_comm_buffer_bytes(void* comm);
+unsigned long long trnopt_comm_epoch(void* comm);
+int trnopt_comm_arrive(void* comm, void* stream);
+int trnopt_comm_wait(void* comm, void* stream);
+int trnopt_comm_destroy(void* comm);
+int trnopt_sinkhorn_run_sharded(void* comm, const void* xpack, const float* xsq, const float* xoff,
+                                const float* log_a, int nx, int sx, const void* ypack, const float* ysq,
+                                const float* yoff, const float* log_b, int ny, int sy, int d, float* g0, float* g1,
+                                float* fh, int start_parity, int n_iter, float eps, float kappa_x, float kappa_y,
+                                void* workspace, size_t ws_bytes, void* stream);
+
+/* Plan evaluation from potentials, float64, for P_ij = exp(log_a_i + log_b_j + (f_i + g_j - C_ij) / eps) with the
+ * direct-difference cost C_ij = sum_k (x_ik - y_jk)^2. x (n, d) and y (m, d) are row-major, already centred and
+ * scaled as the solve saw them ((x - center) / sqrt(cost_scale)); f, g, log_a, log_b may each be NULL (= 0).
+ *
+ * trnopt_plan_rows: out (nrows, m) row-major = the rows P[rows[r], :]; rows (device int array) must lie in [0, n)
+ * (a row index outside gives a row of NaN, nothing out of bounds is read). Replaces the dense host evaluation of
+ * transport_plan (sinkhorn.py:397-403) and wot_tmap (singlecell.py:89-92) for the rows asked for.
+ *
+ * trnopt_plan_log_row_sums: out (n,) = log sum_j P_ij (-inf where the row is all zero), computed as a float64
+ * log-sum-exp; deterministic. Swapping (x, n, f, log_a) with (y, m, g, log_b) gives log column sums. Replaces the
+ * host loops of masses_from_potentials (examples/sinkhorn_libs_compare.py:43-56) and, with log_a = NULL and
+ * log_b = log v, the ancestor pull-back log(P v) (examples/singlecell_figures.py:35-47, before its final
+ * normalisation). Needs a workspace of trnopt_plan_workspace_size(n, m) bytes (8-byte aligned, no
+ * initialisation); one workspace per stream. */
+int trnopt_plan_rows(const double* x, int n, const double* y, int m, int d, const double* f, const double* g,
+                     const double* log_a, const double* log_b, double eps, const int* rows, int nrows, double* out,
+                     void* stream);
+size_t trnopt_plan_workspace_size(int n, int m);
+int trnopt_plan_log_row_sums(const double* x, int n, const double* y, int m, int d, const double* f, const double* g,
+                             const double* log_a, const double* log_b, double eps, double* out, void* workspace,
+                             size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -283,6 +283,39 @@ def plan_marginals(x, y, f, g, eps, center, scale, a=None, b=None, chunk: int = 
     return rows, cols
 
 
+def masses_from_potentials(x, y, a, b, f, g, eps: float, chunk: int = 2048):
+    """examples/sinkhorn_libs_compare.py:43-56: row and column sums of P = a b^T exp((f + g - C) / eps) on clouds
+    that are already normalized, as log-sum-exps over chunks of rows (C expanded as |x|^2 + |y|^2 - 2 x.y)."""
+    from scipy.special import logsumexp
+    x, y, a, b, f, g = (np.asarray(v, dtype=np.float64) for v in (x, y, a, b, f, g))
+    ysq = (y * y).sum(1)
+    rows, cols = np.empty(len(x)), np.full(len(y), -np.inf)
+    for s in range(0, len(x), chunk):
+        xb = x[s:s + chunk]
+        C = (xb * xb).sum(1)[:, None] + ysq[None, :] - 2.0 * (xb @ y.T)
+        S = (f[s:s + chunk, None] + g[None, :] - C) / eps + np.log(a[s:s + chunk])[:, None] + np.log(b)[None, :]
+        rows[s:s + chunk] = np.exp(logsumexp(S, axis=1))
+        cols = np.logaddexp(cols, logsumexp(S, axis=0))
+    return rows, np.exp(cols)
+
+
+def pull_back(x0, x1, f, g, eps, center, scale, log_v1, chunk: int = 1024):
+    """examples/singlecell_figures.py:35-47: log(P v) over x0 for v = exp(log_v1) over x1, with
+    P_ij proportional to exp((f_i + g_j - C_ij) / eps), normalized to log-sum-exp 0."""
+    from scipy.special import logsumexp
+    s = np.sqrt(float(scale))
+    x = (np.asarray(x0, dtype=np.float64) - center) / s
+    y = (np.asarray(x1, dtype=np.float64) - center) / s
+    f, g, lv = (np.asarray(v, dtype=np.float64) for v in (f, g, log_v1))
+    ysq = (y * y).sum(1)
+    out = np.empty(len(x))
+    for i in range(0, len(x), chunk):
+        xb = x[i:i + chunk]
+        C = (xb * xb).sum(1)[:, None] + ysq[None, :] - 2.0 * (xb @ y.T)
+        out[i:i + chunk] = logsumexp((g[None, :] - C) / eps + lv[None, :], axis=1) + f[i:i + chunk] / eps
+    return out - logsumexp(out)
+
+
 # --------------------------------------------------------------------------------------------------------------
 # wot formulation (singlecell.py:46-86)
 # --------------------------------------------------------------------------------------------------------------

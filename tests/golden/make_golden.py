@@ -16,6 +16,10 @@ Files:
                         and the fp64 plan's row / column sums
   normalization.npz     normalization() scales (mean and median, odd and even n m, config 3's full pair)
   wot_small.npz         wot_transport_map() on a reduced config-3 pair (fp64, 3 growth iterations)
+  plan_cases.npz        plan quantities from wot_small's potentials: rows of transport_plan (sinkhorn.py:397-403),
+                        the plan's row / column sums, masses_from_potentials
+                        (examples/sinkhorn_libs_compare.py:43-56) and the ancestor pull-back
+                        (examples/singlecell_figures.py:35-47) for a smooth and a subset-indicator distribution
 """
 
 from __future__ import annotations
@@ -177,8 +181,50 @@ def wot_small():
                         center=r.center, learned=np.stack(tm.learned_growth))
 
 
+def _example(name):
+    """A module of the reference's examples/ folder, loaded by path (its main() is not run)."""
+    src = Path(os.environ.get("TRNOPT_REFERENCE_SRC", "/root/reference/src")).parent / "examples" / f"{name}.py"
+    spec = importlib.util.spec_from_file_location(f"_ref_{name}", src)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def plan_cases():
+    import tempfile
+    z = np.load(HERE / "wot_small.npz")
+    x0, x1, _ = synthetic.cfg3(n=735, m=896)
+    I, J = len(x0), len(x1)
+    r = ref_sk.SinkhornResult(f=z["f"], g=z["g"], iterations=0, error=0.0, converged=True, cost=float("nan"),
+                              seconds=0.0, eps=0.05, rho=(1.0, 50.0), center=z["center"],
+                              cost_scale=float(z["cost_scale"]))
+    a, b = np.full(I, 1.0 / I), np.full(J, 1.0 / J)
+    P = ref_sk.transport_plan(x0, x1, r, a, b)
+    rows = np.array([0, 1, 17, 368, 733, 734])
+    out = dict(rows=rows, plan_rows=P[rows], plan_row_sum=P.sum(1), plan_col_sum=P.sum(0))
+    libs = _example("sinkhorn_libs_compare")
+    s = np.sqrt(float(z["cost_scale"]))
+    xn, yn = (x0 - z["center"]) / s, (x1 - z["center"]) / s
+    out["masses_rows"], out["masses_cols"] = libs.masses_from_potentials(xn, yn, a, b, z["f"], z["g"])
+    figs = _example("singlecell_figures")
+    rng = np.random.default_rng(5)
+    smooth = rng.random(J) + 0.1
+    subset = np.zeros(J)
+    subset[rng.choice(J, 100, replace=False)] = 1.0
+    with tempfile.TemporaryDirectory() as td:
+        pot = Path(td) / "pair.npz"
+        np.savez(pot, x0=x0, x1=x1, center=z["center"], cost_scale=z["cost_scale"], f=z["f"], g=z["g"], eps=0.05)
+        for tag, v in (("smooth", smooth), ("subset", subset)):
+            with np.errstate(divide="ignore"):
+                lv = np.log(v / v.sum())
+            out[f"log_v1_{tag}"] = lv
+            out[f"pull_back_{tag}"] = figs.pull_back_potentials(pot, lv)
+    np.savez_compressed(HERE / "plan_cases.npz", **out)
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["half_step_kat", "row_lse_kat", "solver_cases", "cfg1", "normalization", "wot_small"]
+    which = sys.argv[1:] or ["half_step_kat", "row_lse_kat", "solver_cases", "cfg1", "normalization", "wot_small",
+                             "plan_cases"]
     for w in which:
         print("generating", w, flush=True)
         globals()[w]()

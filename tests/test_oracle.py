@@ -128,3 +128,30 @@ def test_wot_small_matches_reference(golden):
     np.testing.assert_allclose(res.row_mass, z["row_mass"], rtol=1e-9)
     np.testing.assert_allclose(res.col_mass, z["col_mass"], rtol=1e-9)
     np.testing.assert_allclose(res.f, z["f"], rtol=0, atol=1e-9)
+
+
+def _wot_small_result(z):
+    return O.Result(f=z["f"], g=z["g"], iterations=0, error=0.0, converged=True, cost=float("nan"), seconds=0.0,
+                    eps=0.05, rho=(1.0, 50.0), center=z["center"], cost_scale=float(z["cost_scale"]))
+
+
+def test_plan_functions_match_reference(golden):
+    """Oracle plan rows, plan sums, masses_from_potentials and the ancestor pull-back against the reference's own
+    transport_plan and example functions on wot_small's potentials."""
+    z, p = golden("wot_small.npz"), golden("plan_cases.npz")
+    x0, x1, _ = synthetic.cfg3(n=735, m=896)
+    I, J = len(x0), len(x1)
+    r = _wot_small_result(z)
+    a, b = np.full(I, 1.0 / I), np.full(J, 1.0 / J)
+    P = O.transport_plan(x0, x1, r, a, b)
+    np.testing.assert_allclose(P[p["rows"]], p["plan_rows"], rtol=1e-12, atol=0)
+    rows, cols = O.plan_marginals(x0, x1, r.f, r.g, 0.05, r.center, r.cost_scale, a, b)
+    np.testing.assert_allclose(rows, p["plan_row_sum"], rtol=1e-10)
+    np.testing.assert_allclose(cols, p["plan_col_sum"], rtol=1e-10)
+    s = np.sqrt(r.cost_scale)
+    mr, mc = O.masses_from_potentials((x0 - r.center) / s, (x1 - r.center) / s, a, b, r.f, r.g, 0.05)
+    np.testing.assert_allclose(mr, p["masses_rows"], rtol=1e-12)
+    np.testing.assert_allclose(mc, p["masses_cols"], rtol=1e-12)
+    for tag in ("smooth", "subset"):
+        pb = O.pull_back(x0, x1, r.f, r.g, 0.05, r.center, r.cost_scale, p[f"log_v1_{tag}"])
+        np.testing.assert_allclose(pb, p[f"pull_back_{tag}"], rtol=0, atol=1e-10)

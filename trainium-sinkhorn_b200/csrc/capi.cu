@@ -90,6 +90,34 @@ int ffma_run(LseProblem& p, void* ws, size_t ws_bytes, cudaStream_t stream) {
 
 }  // namespace
 
+namespace trnopt {
+
+int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
+                        const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
+                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub) {
+  if (!tc_supported_d(d)) return TRNOPT_ERR_UNSUPPORTED;
+  if (!xpack || !ypack || !xsq || !gh || !log_b || !fh || rows < 1 || m < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned(xpack, 128) || !aligned(ypack, 128)) return TRNOPT_ERR_ALIGNMENT;
+  if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  if (device_cc_major(dev) != 10) return TRNOPT_ERR_UNSUPPORTED;
+  LseProblem p{};
+  p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off; p.rows = rows; p.m = m; p.d = d;
+  const double inv_eps = 1.0 / (double)eps;
+  p.dot2 = (float)(2.0 * inv_eps * 1.4426950408889634);
+  p.gh2 = (float)(inv_eps * 1.4426950408889634);
+  p.lb2 = kLog2e;
+  p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
+  StreamK sk{};
+  tc_plan(dev, rows, m, d, sk);
+  int st = bind_workspace(sk, tc_partial_bytes(sk), workspace, ws_bytes);
+  if (st != TRNOPT_OK) return st;
+  p.error_word = device_error_word();
+  return cuda_status(tc_launch(p, xpack, ypack, sx, sy, sk, stream, pub));
+}
+
+}  // namespace trnopt
+
 extern "C" {
 
 int trnopt_version(void) { return 100; }
@@ -198,25 +226,8 @@ int trnopt_pack_cloud(const float* xT, int ldx, int n, int d, int scale_exp, voi
 int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
                         const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
                         void* workspace, size_t ws_bytes, void* stream) {
-  if (!tc_supported_d(d)) return TRNOPT_ERR_UNSUPPORTED;
-  if (!xpack || !ypack || !xsq || !gh || !log_b || !fh || rows < 1 || m < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
-  if (!aligned(xpack, 128) || !aligned(ypack, 128)) return TRNOPT_ERR_ALIGNMENT;
-  if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
-  const int dev = current_device();
-  if (device_cc_major(dev) != 10) return TRNOPT_ERR_UNSUPPORTED;
-  LseProblem p{};
-  p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off; p.rows = rows; p.m = m; p.d = d;
-  const double inv_eps = 1.0 / (double)eps;
-  p.dot2 = (float)(2.0 * inv_eps * 1.4426950408889634);
-  p.gh2 = (float)(inv_eps * 1.4426950408889634);
-  p.lb2 = kLog2e;
-  p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
-  StreamK sk{};
-  tc_plan(dev, rows, m, d, sk);
-  int st = bind_workspace(sk, tc_partial_bytes(sk), workspace, ws_bytes);
-  if (st != TRNOPT_OK) return st;
-  p.error_word = device_error_word();
-  return cuda_status(tc_launch(p, xpack, ypack, sx, sy, sk, reinterpret_cast<cudaStream_t>(stream)));
+  return half_step_tc_launch(xpack, xsq, off, ypack, gh, log_b, rows, m, d, sx, sy, eps, kappa, fh, workspace,
+                             ws_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr);
 }
 
 int trnopt_test_ex2_poly(const float* x, float* out, int n, void* stream) {
@@ -277,6 +288,37 @@ int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float*
 int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream) {
   if (!gh_old || !gh_new || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
   return cuda_status(max_change_launch(gh_old, gh_new, n, inv_eps, out, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+static bool plan_args_ok(const double* x, int n, const double* y, int m, int d, double eps) {
+  return x && y && n >= 1 && m >= 1 && d >= 1 && eps > 0.0 && isfinite(eps);
+}
+
+int trnopt_plan_rows(const double* x, int n, const double* y, int m, int d, const double* f, const double* g,
+                     const double* log_a, const double* log_b, double eps, const int* rows, int nrows, double* out,
+                     void* stream) {
+  if (!plan_args_ok(x, n, y, m, d, eps) || nrows < 0 || (nrows > 0 && (!rows || !out)))
+    return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (nrows == 0) return TRNOPT_OK;
+  if (!aligned(x, 8) || !aligned(y, 8) || !aligned(out, 8) || !aligned(rows, 4)) return TRNOPT_ERR_ALIGNMENT;
+  return cuda_status(plan_rows_launch(x, n, y, m, d, f, g, log_a, log_b, eps, rows, nrows, out,
+                                      reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t trnopt_plan_workspace_size(int n, int m) {
+  if (n < 1 || m < 1) return 0;
+  return plan_lse_workspace_bytes(current_device(), n, m);
+}
+
+int trnopt_plan_log_row_sums(const double* x, int n, const double* y, int m, int d, const double* f, const double* g,
+                             const double* log_a, const double* log_b, double eps, double* out, void* workspace,
+                             size_t ws_bytes, void* stream) {
+  if (!plan_args_ok(x, n, y, m, d, eps) || !out) return TRNOPT_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  if (workspace == nullptr || ws_bytes < plan_lse_workspace_bytes(dev, n, m)) return TRNOPT_ERR_WORKSPACE;
+  if (!aligned(x, 8) || !aligned(y, 8) || !aligned(out, 8) || !aligned(workspace, 8)) return TRNOPT_ERR_ALIGNMENT;
+  return cuda_status(plan_lse_launch(dev, x, n, y, m, d, f, g, log_a, log_b, eps, out, workspace,
+                                     reinterpret_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

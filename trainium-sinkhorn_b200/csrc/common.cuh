@@ -34,6 +34,7 @@ enum ErrorBits : int {
   kErrWaitTimeout = 1,   // an mbarrier / pipeline wait ran out of its time limit
   kErrTmemAlloc = 2,     // tensor-memory allocation did not return in time
   kErrBadLaunch = 4,     // a launch-shape invariant did not hold on the device
+  kErrPeerTimeout = 8,   // another GPU of the job did not publish its rows within the time limit
 };
 
 struct LseProblem {
@@ -96,7 +97,7 @@ __device__ __forceinline__ void lse_merge(float& M, float& l, float M2, float l2
 
 // Finish one row: merge nparts partials (M, l) in double precision and apply the kappa / off epilogue
 // (reference src/trnopt/sinkhorn.py:119, src/trnopt/nki_sinkhorn.py:212-225).
-__device__ inline void finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride) {
+__device__ inline float finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride) {
   float M = kMaxFloor;
   for (int s = 0; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
   double l = 0.0;
@@ -114,6 +115,7 @@ __device__ inline void finish_row(const LseProblem& p, int row, const float2* pa
     res = lse;
   }
   p.out[row] = (float)res;
+  return (float)res;
 }
 
 // Bounded-wait helpers ---------------------------------------------------------------------------------------
@@ -125,5 +127,72 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;   // 4 s: no legitimate wait in these kernels is close
+
+// Publishing a half-step's rows to the other GPUs of a job ------------------------------------------------------
+//
+// With one process per GPU and the rows of a half-step split over the GPUs, every GPU needs the whole new potential
+// before the next half-step. Instead of an all-gather after the kernel, the kernel's epilogue stores each finished
+// row into every GPU's copy of the output vector (peer memory over NVLink), and the last CTA to finish raises this
+// GPU's flag in every other GPU's flag array to the launch's epoch. A later launch reads its input only after every
+// other GPU's flag has reached the epoch it depends on. The flags live in each GPU's own memory; slot q of a GPU's
+// array is written only by GPU q.
+constexpr int kMaxRanks = 8;
+
+struct Publish {
+  int world;                                   // GPUs in the job; 1 = nothing to publish or wait for
+  int rank;                                    // this GPU's index in the job
+  float* out_peer[kMaxRanks];                  // this launch's output rows as mapped in each GPU's copy
+  unsigned long long* flag_peer[kMaxRanks];    // slot `rank` of each GPU's flag array
+  const unsigned long long* flags;             // this GPU's flag array (slot q written by GPU q)
+  unsigned long long wait_epoch;               // the input is complete once every other slot is >= wait_epoch
+  unsigned long long epoch;                    // written to every other GPU when this launch is complete
+  int* done;                                   // CTAs of this launch that have finished (zero between launches)
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Wait (one thread) until every other GPU's slot reaches pub.wait_epoch. Bounded: false after kWaitLimitNs, with
+// kErrPeerTimeout set in the error word.
+__device__ inline bool wait_peers(const Publish& pub, int* error_word) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (int q = 0; q < pub.world; ++q) {
+    if (q == pub.rank) continue;
+    while (ld_acquire_sys(pub.flags + q) < pub.wait_epoch) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(error_word, (int)kErrPeerTimeout);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+// Store one finished row into the other GPUs' copies (the local copy is written by finish_row).
+__device__ __forceinline__ void publish_row(const Publish& pub, int row, float v) {
+  for (int q = 0; q < pub.world; ++q)
+    if (q != pub.rank) pub.out_peer[q][row] = v;
+}
+
+// Called by one thread of each CTA after the CTA's last publish_row (every writer has executed
+// __threadfence_system() and passed a CTA barrier since). The last CTA of the grid raises this GPU's slot to
+// pub.epoch on every other GPU and re-arms the counter.
+__device__ inline void publish_done(const Publish& pub) {
+  __threadfence_system();
+  if (atomicAdd(pub.done, 1) == (int)gridDim.x - 1) {
+    __threadfence_system();
+    for (int q = 0; q < pub.world; ++q)
+      if (q != pub.rank) st_release_sys(pub.flag_peer[q], pub.epoch);
+    atomicExch(pub.done, 0);
+  }
+}
 
 }  // namespace trnopt

@@ -355,6 +355,7 @@ struct TcArgs {
   LseProblem p;
   StreamK sk;
   int dk;            // elements of each half (hi, lo) per packed row; multiple of 16
+  Publish pub;       // world > 1: wait for the other GPUs' rows of gh, publish this GPU's rows of the output
 };
 
 template <int NKB>
@@ -473,13 +474,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the previous grid (which may write gh) is complete
     int T = 0;
     bool ok = true;
+    if (args.pub.world > 1) {
+      // gh is complete once every other GPU has published its rows of it (their stores land in this GPU's copy;
+      // the loads below go through L2, never a stale L1 line)
+      int w = 1;
+      if (lane == 0) w = wait_peers(args.pub, p.error_word) ? 1 : 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!w) {
+        *abort_flag = 1;
+        ok = false;
+      }
+    }
     for (long long u = u_begin; u < u_end && ok; ++u, ++T) {
       const int c = (int)(u % sk.nct);
       float g[TC_BN / 32], l[TC_BN / 32];
 #pragma unroll
       for (int q = 0; q < TC_BN / 32; ++q) {
         const int j = c * TC_BN + q * 32 + lane;
-        g[q] = j < p.m ? __ldg(ghp + j) : 0.f;
+        g[q] = j < p.m ? __ldcg(ghp + j) : 0.f;
         l[q] = j < p.m ? __ldg(lbp + j) : -INFINITY;
       }
       const int bslot = T % TC_NBIAS;
@@ -582,10 +594,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (s_last[wg]) {
         __threadfence();
         const int row = r * TC_BM + qrow;
-        if (row < p.rows) finish_row(p, row, base + qrow, expected, TC_BM);
+        if (row < p.rows) {
+          const float v = finish_row(p, row, base + qrow, expected, TC_BM);
+          if (args.pub.world > 1) publish_row(args.pub, row, v);
+        }
         if (qrow == 0) sk.counters[r] = 0;
       }
     }
+    if (args.pub.world > 1) __threadfence_system();   // this thread's peer stores, before the CTA barrier below
   }
 
   tmem_fence_before();
@@ -594,6 +610,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tmem_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
   }
+  if (args.pub.world > 1 && threadIdx.x == 0) publish_done(args.pub);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -742,7 +759,7 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
 }
 
 cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const Publish* pub) {
   const int kp = tc_kp(p.d);
   CUtensorMap ma, mb;
   if (!tensor_map(xpack, p.rows, kp, TC_BM, &ma) || !tensor_map(ypack, p.m, kp, TC_BN, &mb))
@@ -752,6 +769,12 @@ cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack,
   a.p.dot2 = (float)((double)p.dot2 * ldexp(1.0, -(sx + sy)));
   a.sk = sk;
   a.dk = tc_dk(p.d);
+  if (pub) {
+    a.pub = *pub;
+  } else {
+    a.pub = Publish{};
+    a.pub.world = 1;
+  }
   if (kp == 64) return tc_launch_t<1>(ma, mb, a, stream);
   return tc_launch_t<2>(ma, mb, a, stream);
 }

@@ -22,7 +22,7 @@ void tc_plan(int device, int rows, int m, int d, StreamK& sk);
 size_t tc_partial_bytes(const StreamK& sk);
 cudaError_t tc_pack(const float* xT, int ldx, int n, int d, int scale_exp, void* packed, cudaStream_t stream);
 cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const Publish* pub = nullptr);
 
 // companions (companions.cu)
 cudaError_t balanced_error_launch(const float* gh_old, const float* gh_new, const float* w, int n, float inv_eps,
@@ -35,8 +35,23 @@ size_t median_workspace_bytes();
 cudaError_t median_launch(const double* x, const double* y, const double* sqx, const double* sqy, int n, int m,
                           int d, double* out, void* ws, cudaStream_t stream);
 
+// plan evaluation from potentials, float64 (plan.cu)
+int plan_lse_splits(int device, int n, int m);
+size_t plan_lse_workspace_bytes(int device, int n, int m);
+cudaError_t plan_rows_launch(const double* x, int n, const double* y, int m, int d, const double* f, const double* g,
+                             const double* la, const double* lb, double eps, const int* rows, int nrows, double* out,
+                             cudaStream_t stream);
+cudaError_t plan_lse_launch(int device, const double* x, int n, const double* y, int m, int d, const double* f,
+                            const double* g, const double* la, const double* lb, double eps, double* out, void* ws,
+                            cudaStream_t stream);
+
 cudaError_t ex2_poly_launch(const float* x, float* out, int n, cudaStream_t stream);
 
 int* device_error_word();
+
+// The tcgen05 half-step behind trnopt_half_step_tc, with an optional Publish (capi.cu); returns a TRNOPT status.
+int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
+                        const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
+                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub);
 
 }  // namespace trnopt

@@ -31,7 +31,7 @@ def _load():
 
 lib = _load()
 
-_P, _I, _F, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+_P, _I, _F, _D, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_double, ctypes.c_size_t
 _SIGS = {
     "trnopt_version": (_I, []),
     "trnopt_status_string": (ctypes.c_char_p, [_I]),
@@ -53,6 +53,20 @@ _SIGS = {
                                  _F, _F, _F, _P, _Z, _P]),
     "trnopt_median_workspace_size": (_Z, []),
     "trnopt_median_cost": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
+    "trnopt_comm_handle_bytes": (_Z, []),
+    "trnopt_comm_create": (_I, [_I, _I, _Z, ctypes.POINTER(_P), _P]),
+    "trnopt_comm_open": (_I, [_P, _P]),
+    "trnopt_comm_buffer": (_P, [_P]),
+    "trnopt_comm_buffer_bytes": (_Z, [_P]),
+    "trnopt_comm_epoch": (ctypes.c_ulonglong, [_P]),
+    "trnopt_comm_arrive": (_I, [_P, _P]),
+    "trnopt_comm_wait": (_I, [_P, _P]),
+    "trnopt_comm_destroy": (_I, [_P]),
+    "trnopt_sinkhorn_run_sharded": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I,
+                                         _F, _F, _F, _P, _Z, _P]),
+    "trnopt_plan_rows": (_I, [_P, _I, _P, _I, _I, _P, _P, _P, _P, _D, _P, _I, _P, _P]),
+    "trnopt_plan_workspace_size": (_Z, [_I, _I]),
+    "trnopt_plan_log_row_sums": (_I, [_P, _I, _P, _I, _I, _P, _P, _P, _P, _D, _P, _P, _Z, _P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -200,6 +214,55 @@ def sinkhorn_run(path, x_op, ldx, xsq, xoff, log_a, nx, sx, y_op, ldy, ysq, yoff
                                   ldy, _ptr(ysq), _ptr(yoff), _ptr(log_b), ny, int(sy), d, _ptr(g0), _ptr(g1),
                                   _ptr(fh), int(start_parity), int(n_iter), float(eps), float(kappa_x),
                                   float(kappa_y), _ptr(ws), ws.numel(), _stream()), "trnopt_sinkhorn_run")
+
+
+def _plan_args(x, y, f, g, log_a, log_b):
+    _need(x, "x", torch.float64)
+    _need(y, "y", torch.float64)
+    if x.dim() != 2 or y.dim() != 2 or x.shape[1] != y.shape[1]:
+        raise ValueError("x (n, d) and y (m, d) must share d")
+    for t, nm, n in ((f, "f", x.shape[0]), (g, "g", y.shape[0]), (log_a, "log_a", x.shape[0]),
+                     (log_b, "log_b", y.shape[0])):
+        if t is not None:
+            _need(t, nm, torch.float64)
+            if t.shape != (n,):
+                raise ValueError(f"{nm} must have shape ({n},)")
+
+
+def plan_rows(x, y, f, g, log_a, log_b, eps, rows: torch.Tensor) -> torch.Tensor:
+    """Rows P[rows, :] of P = exp(log_a + log_b^T + (f + g^T - C) / eps), float64 (n, d) / (m, d) clouds."""
+    _plan_args(x, y, f, g, log_a, log_b)
+    _need(rows, "rows", torch.int32)
+    n, d = x.shape
+    m = y.shape[0]
+    out = torch.empty((rows.numel(), m), dtype=torch.float64, device=x.device)
+    check(lib.trnopt_plan_rows(_ptr(x), n, _ptr(y), m, d, _ptr(f), _ptr(g), _ptr(log_a), _ptr(log_b), float(eps),
+                               _ptr(rows), rows.numel(), _ptr(out), _stream()), "trnopt_plan_rows")
+    return out
+
+
+def plan_log_row_sums(x, y, f, g, log_a, log_b, eps) -> torch.Tensor:
+    """log sum_j P_ij for every row i, float64."""
+    _plan_args(x, y, f, g, log_a, log_b)
+    n, d = x.shape
+    m = y.shape[0]
+    ws = torch.empty(max(8, int(lib.trnopt_plan_workspace_size(n, m))), dtype=torch.uint8, device=x.device)
+    out = torch.empty(n, dtype=torch.float64, device=x.device)
+    check(lib.trnopt_plan_log_row_sums(_ptr(x), n, _ptr(y), m, d, _ptr(f), _ptr(g), _ptr(log_a), _ptr(log_b),
+                                       float(eps), _ptr(out), _ptr(ws), ws.numel(), _stream()),
+          "trnopt_plan_log_row_sums")
+    return out
+
+
+def sinkhorn_run_sharded(comm, xpack, xsq, xoff, log_a, nx, sx, ypack, ysq, yoff, log_b, ny, sy, d, g0, g1, fh,
+                         start_parity, n_iter, eps, kappa_x, kappa_y, ws) -> None:
+    """Queue n_iter iterations over row shards, each half-step publishing its rows to every rank (comm: a
+    trnopt_comm handle; g0, g1, fh in its buffer)."""
+    check(lib.trnopt_sinkhorn_run_sharded(comm, _ptr(xpack), _ptr(xsq), _ptr(xoff), _ptr(log_a), nx, int(sx),
+                                          _ptr(ypack), _ptr(ysq), _ptr(yoff), _ptr(log_b), ny, int(sy), d, _ptr(g0),
+                                          _ptr(g1), _ptr(fh), int(start_parity), int(n_iter), float(eps),
+                                          float(kappa_x), float(kappa_y), _ptr(ws), ws.numel(), _stream()),
+          "trnopt_sinkhorn_run_sharded")
 
 
 def device_error_flags() -> int:

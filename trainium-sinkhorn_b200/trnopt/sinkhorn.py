@@ -57,6 +57,8 @@ class SinkhornOptions:
     kernel: str = "auto"           # "auto" / "cuda": the fused CUDA half-step (the only one in this package)
     backend: Backend = Backend.preset("cuda-fused")
     cuda_path: str = "auto"        # "tc": tcgen05 split-precision kernel (d <= 64), "ffma": FP32 FFMA tile kernel
+    cuda_exchange: str = "auto"    # cores > 1: "peer" (half-steps store their rows into every GPU's copy over
+                                   # NVLink; tc path), "nccl" (all-gather after each half-step); auto = peer on tc
                                    #   (any d <= 128), "auto": tc where it applies
 
 
@@ -102,6 +104,18 @@ def _resolve_path(path: str, d: int) -> str:
     if path == "auto":
         return "tc" if tc_ok else "ffma"
     return path
+
+
+def _exchange(how: str, path: str) -> str:
+    """How the row shards of a half-step reach every GPU: "peer" (stored into every GPU's copy by the kernel that
+    computes them; tc path) or "nccl" (an all-gather after the kernel)."""
+    if how not in ("auto", "peer", "nccl"):
+        raise ValueError(f"cuda_exchange={how!r}: choose 'auto', 'peer' or 'nccl'")
+    if how == "peer" and path != "tc":
+        raise ValueError("cuda_exchange='peer' needs the tc path")
+    if how == "auto":
+        return "peer" if path == "tc" else "nccl"
+    return how
 
 
 def _scale_exp(P: np.ndarray) -> int:
@@ -241,15 +255,27 @@ class _Off:
 class _Runs:
     """Runs of n iterations (f then g half-step each) at one (eps, kappa_x, kappa_y). On one GPU a run is queued by a
     single C call (trnopt_sinkhorn_run: the loop body of sinkhorn.py:353-354 issued from C), so the host costs one
-    call per run between checks instead of two per iteration. With row shards the run goes half-step by half-step,
-    each followed by its NCCL all-gather."""
+    call per run between checks instead of two per iteration. With row shards and a peer region (peer exchange),
+    the run is one C call too (trnopt_sinkhorn_run_sharded): each half-step stores its rows into every GPU's copy
+    and the GPUs order themselves by epochs. Otherwise (nccl exchange) the run goes half-step by half-step, each
+    followed by its NCCL all-gather."""
 
-    def __init__(self, step, X, Y, G, fh, use_off: bool = True):
-        self.step, self.X, self.Y, self.G, self.fh = step, X, Y, G, fh
+    def __init__(self, step, X, Y, G, fh, peer=None):
+        self.step, self.X, self.Y, self.G, self.fh, self.peer = step, X, Y, G, fh, peer
         self.fused = step.shards == 1
+
+    def sync(self) -> None:
+        """Before anything outside the runs reads G or fh: every rank's rows of the last run are in."""
+        if self.peer is not None:
+            self.peer.wait()
 
     def run(self, it, n, e, kx, ky):
         X, Y, G, fh, st = self.X, self.Y, self.G, self.fh, self.step
+        if self.peer is not None:
+            _capi.sinkhorn_run_sharded(self.peer.comm, X.packed, X.sq, X.off, X.log_w, X.npad, X.sexp, Y.packed, Y.sq,
+                                       Y.off, Y.log_w, Y.npad, Y.sexp, X.d, G[0], G[1], fh, it % 2, n, e, kx, ky,
+                                       st.ws)
+            return
         if not self.fused:
             for i in range(it, it + n):
                 st(X, Y, G[i % 2], e, kx, out=fh)
@@ -346,10 +372,21 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         gh0 = np.zeros(Y.npad)
         gh0[:Y.n] = (ys * ys).sum(1) - (yi * yi).sum(1)
         # Ping-pong potentials: before iteration i the shifted g is G[i % 2]; fh has one buffer.
-        G = [torch.as_tensor(gh0, dtype=torch.float32).to(dev), torch.empty(Y.npad, dtype=torch.float32, device=dev)]
-        fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
+        peer = None
+        if shards > 1 and _exchange(opts.cuda_exchange, path) == "peer":
+            from . import _comm
+            peer = _comm.region(4 * (X.npad + 2 * Y.npad), group)
+            fh = peer.tensor(0, X.npad)
+            G = [peer.tensor(4 * X.npad, Y.npad), peer.tensor(4 * (X.npad + Y.npad), Y.npad)]
+            G[0].copy_(torch.as_tensor(gh0, dtype=torch.float32))
+            fh.zero_()
+            peer.arrive()                                  # the others may write into these buffers from here on
+        else:
+            G = [torch.as_tensor(gh0, dtype=torch.float32).to(dev),
+                 torch.empty(Y.npad, dtype=torch.float32, device=dev)]
+            fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
         err_dev = torch.zeros(1, dtype=torch.float32, device=dev)
-        runner = _Runs(step, X, Y, G, fh)
+        runner = _Runs(step, X, Y, G, fh, peer)
         err, converged, it = float("nan"), False, 0
         stage, stage_it = 0, 0
         stage_tol = max(opts.stage_tol, 1e-5)              # float32 floors (sinkhorn.py:342-344)
@@ -369,6 +406,7 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
                 n = opts.check_every - (stage_it % opts.check_every)
             n = min(n, opts.max_iters - it)
             runner.run(it, n, e, kap(e, rho_x), kap(e, rho_y))
+            runner.sync()
             it += n
             stage_it += n
             gh_prev, gh_new = G[(it - 1) % 2], G[it % 2]
@@ -412,10 +450,7 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
 
 
 def transport_plan(x, y, res: SinkhornResult, a=None, b=None) -> np.ndarray:
-    """The dense plan P (n x m, float64) from a result, on the host: for small problems and tests only
-    (sinkhorn.py:397-403)."""
-    x = (np.asarray(x, dtype=np.float64) - res.center) / np.sqrt(res.cost_scale)
-    y = (np.asarray(y, dtype=np.float64) - res.center) / np.sqrt(res.cost_scale)
-    log_a, log_b = _log_weights(a, len(x), "a"), _log_weights(b, len(y), "b")
-    C = ((x[:, None, :] - y[None, :, :]) ** 2).sum(axis=2)
-    return np.exp(log_a[:, None] + log_b[None, :] + (res.f[:, None] + res.g[None, :] - C) / res.eps)
+    """The dense plan P (n x m, float64) from a result: for small problems and tests only (sinkhorn.py:397-403).
+    Evaluated in float64 by the library's plan kernel (trnopt.plan)."""
+    from .plan import transport_plan as _plan
+    return _plan(x, y, res, a, b)
