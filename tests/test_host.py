@@ -122,3 +122,16 @@ def test_synthetic_generators_are_seeded():
     assert len(tr.cohorts) == 39 and abs(sum(len(c) for c in tr.cohorts) - 175_000) < 100
     stages = synthetic.cfg5_eps_stages()
     assert len(stages) == 7 and stages[0] == 1.0 and abs(stages[-1] / 0.01 - (1 / 0.01) ** (1 / 7)) < 1e-9
+
+
+def test_exchange_selection():
+    """cores > 1: peer stores on the tc path by default, the NCCL all-gather on the FFMA path; bad names raise."""
+    import trnopt.sinkhorn  # noqa: F401
+    S = sys.modules["trnopt.sinkhorn"]
+    assert S._exchange("auto", "tc") == "peer"
+    assert S._exchange("auto", "ffma") == "nccl"
+    assert S._exchange("nccl", "tc") == "nccl"
+    with pytest.raises(ValueError):
+        S._exchange("peer", "ffma")
+    with pytest.raises(ValueError):
+        S._exchange("mpi", "tc")
