@@ -22,6 +22,7 @@
 // Every mbarrier wait is bounded (common.cuh kWaitLimitNs); a timeout sets the device error word and the CTA
 // unwinds (waits for its own copies and MMAs, frees TMEM) instead of hanging.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -36,7 +37,7 @@ constexpr int TC_BM = 128;          // rows per tile (MMA M, TMEM lanes)
 constexpr int TC_BN = 256;          // columns per tile (MMA N)
 constexpr int TC_NACC = 2;          // TMEM accumulators of TC_BN columns (512 columns in all)
 constexpr int TC_THREADS = 352;     // 8 epilogue warps + TMA producer + MMA + bias
-constexpr int TC_NBIAS = 8;         // bias ring slots
+constexpr int TC_NBB = 2;           // column-bias operand slots (one per tile in flight between bias warp and MMA)
 constexpr int TC_PRODUCER_WARP = 8;
 constexpr int TC_MMA_WARP = 9;
 constexpr int TC_BIAS_WARP = 10;
@@ -157,22 +158,15 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// One block of 64 values of a row after the bias FMA, relative to `shift` (0 for a row's first block): the max and,
-// for a row past its first block, the lazy sum 2^(a_j) (exps relative to the running M = shift).
+// One block of 64 values of a row relative to `shift` (0 for a row's first block): u_j = acc_j * dot2 - shift (the
+// column bias is already in the accumulator), their max, and the values themselves in a[].
 template <int N>
-__device__ __forceinline__ void block_terms(uint32_t (&v)[N], const float* bh, uint64_t d2, float shift, float (&a)[N],
-                                            float& cmax) {
+__device__ __forceinline__ void block_terms(uint32_t (&v)[N], uint64_t d2, float shift, float (&a)[N], float& cmax) {
   const uint64_t nm = pk2(-shift, -shift);
-  const float4* b4 = reinterpret_cast<const float4*>(bh);
 #pragma unroll
-  for (int q = 0; q < N / 4; ++q) {
-    const float4 b = b4[q];
-    const uint64_t u0 =
-        ffma2(pk2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])), d2, fadd2(pk2(b.x, b.y), nm));
-    const uint64_t u1 =
-        ffma2(pk2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])), d2, fadd2(pk2(b.z, b.w), nm));
-    upk2(u0, a[4 * q], a[4 * q + 1]);
-    upk2(u1, a[4 * q + 2], a[4 * q + 3]);
+  for (int q = 0; q < N / 2; ++q) {
+    const uint64_t u = ffma2(pk2(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1])), d2, nm);
+    upk2(u, a[2 * q], a[2 * q + 1]);
   }
   float c[4];                                                 // chain k reduces every fourth group of 8
 #pragma unroll
@@ -225,32 +219,28 @@ __device__ __forceinline__ float exp_sum(const float (&a)[N], float off) {
   return x0 + x1;
 }
 
-// Redo of one block in absolute terms from the raw accumulators re-read from TMEM (into the registers of a[]).
-// The relative values lose their low bits when M is far below the block (e.g. M set by columns of PAD_LOG_WEIGHT,
-// -1e9). Warp-uniform entry (tcgen05.ld is .sync.aligned); only lanes with `redo` change (M, L).
-template <int N>
-__device__ __forceinline__ void block_redo(uint32_t taddr, const float* bh, float dot2, bool redo, float (&a)[N],
-                                           float& M, float& L) {
-  uint32_t* raw = reinterpret_cast<uint32_t*>(a);
+// Redo of one 64-value block in absolute terms from the raw accumulators re-read from TMEM; returns the new
+// (M, L). The relative values lose their low bits when M is far below the block (e.g. M set by columns of
+// PAD_LOG_WEIGHT, -1e9). Warp-uniform entry (tcgen05.ld is .sync.aligned); lanes without `redo` get (M, L) back
+// unchanged.
+__device__ __forceinline__ float2 block_redo(uint32_t taddr, float dot2, bool redo, float M, float L) {
+  constexpr int N = 64;
+  uint32_t raw[N];
   TRNOPT_TMEM_LD64(taddr, raw);
   tmem_wait_ld();
-#pragma unroll
-  for (int j = 0; j < N; ++j) asm volatile("" : "+r"(raw[j]));
-  if (!redo) return;
-  const float4* b4 = reinterpret_cast<const float4*>(bh);
+  if (!redo) return make_float2(M, L);
+  float a[N];
   float tmax = kMaxFloor;
 #pragma unroll
   for (int q = 0; q < N / 4; ++q) {
-    const float4 b = b4[q];
-    a[4 * q + 0] = fmaf(__uint_as_float(raw[4 * q + 0]), dot2, b.x);
-    a[4 * q + 1] = fmaf(__uint_as_float(raw[4 * q + 1]), dot2, b.y);
-    a[4 * q + 2] = fmaf(__uint_as_float(raw[4 * q + 2]), dot2, b.z);
-    a[4 * q + 3] = fmaf(__uint_as_float(raw[4 * q + 3]), dot2, b.w);
+    a[4 * q + 0] = __uint_as_float(raw[4 * q + 0]) * dot2;
+    a[4 * q + 1] = __uint_as_float(raw[4 * q + 1]) * dot2;
+    a[4 * q + 2] = __uint_as_float(raw[4 * q + 2]) * dot2;
+    a[4 * q + 3] = __uint_as_float(raw[4 * q + 3]) * dot2;
     tmax = fmaxf(tmax, fmaxf(fmaxf(a[4 * q], a[4 * q + 1]), fmaxf(a[4 * q + 2], a[4 * q + 3])));
   }
   const float Mn = tmax + kLazyHeadroom;
-  L = L * ex2_approx(M - Mn) + exp_sum(a, Mn);
-  M = Mn;
+  return make_float2(Mn, L * ex2_approx(M - Mn) + exp_sum(a, Mn));
 }
 
 // Lazy-max update of (M, L) with a block whose values a[] are relative to M (not a first block): the exps use the
@@ -281,13 +271,12 @@ __device__ __forceinline__ void block_first(const float (&a)[N], float cmax, flo
 }
 
 // Fold one row's 128 accumulator values of a tile (TMEM address taddr, 32x32b lanes: this thread's row) into the
-// row's running base-2 (M, L):   t_j = acc_j * dot2 + bias_j,   L = sum_j 2^(t_j - M).
-// Two blocks of 64 values (u_j = t_j - M from one packed FMA, acc * dot2 + (bias - M)). Block 1 is loaded from TMEM
+// row's running base-2 (M, L):   t_j = acc_j * dot2 (the accumulator holds x.y plus the column bias / dot2),
+// L = sum_j 2^(t_j - M). Two blocks of 64 values (u_j = t_j - M from one packed FMA, acc * dot2 - M). Block 1 is loaded from TMEM
 // while block 0's exps run; once block 1 is loaded and its max (and any redo re-read) is done, every TMEM read of
 // the tile is over and the accumulator is released (tcgen05 fence, then an arrival on `acc_empty`) before block 1's
 // exps, so the MMAs two tiles ahead overlap them. Must be called by all 32 lanes of the warp.
-__device__ __forceinline__ void lse_tile128(uint32_t taddr, const float* bias, float dot2, float& M, float& L,
-                                            uint64_t* acc_empty) {
+__device__ __forceinline__ void lse_tile128(uint32_t taddr, float dot2, float& M, float& L, uint64_t* acc_empty) {
   constexpr int N = 64;
   const uint64_t d2 = pk2(dot2, dot2);
   uint32_t v[N];
@@ -299,7 +288,7 @@ __device__ __forceinline__ void lse_tile128(uint32_t taddr, const float* bias, f
   for (int j = 0; j < N; ++j) asm volatile("" : "+r"(v[j]));
   // block 0
   bool first = (M == kMaxFloor);
-  block_terms(v, bias, d2, first ? 0.f : M, a, cmax);
+  block_terms(v, d2, first ? 0.f : M, a, cmax);
   TRNOPT_TMEM_LD64(taddr + (uint32_t)N, v);                   // block 1 into the now-free registers
   bool redo = false;
   if (first) block_first(a, cmax, M, L);
@@ -307,17 +296,23 @@ __device__ __forceinline__ void lse_tile128(uint32_t taddr, const float* bias, f
   tmem_wait_ld();
 #pragma unroll
   for (int j = 0; j < N; ++j) asm volatile("" : "+r"(v[j]));
-  if (__any_sync(0xffffffffu, redo)) block_redo(taddr, bias, dot2, redo, a, M, L);
+  if (__any_sync(0xffffffffu, redo)) {
+    const float2 r = block_redo(taddr, dot2, redo, M, L);
+    M = r.x;
+    L = r.y;
+  }
   // block 1: terms and max, then its redo re-read if any, then release the accumulator, then the exps
   first = (M == kMaxFloor);
-  block_terms(v, bias + N, d2, first ? 0.f : M, a, cmax);
+  block_terms(v, d2, first ? 0.f : M, a, cmax);
   redo = !first && cmax > kLazyRedo;
   if (__any_sync(0xffffffffu, redo)) {
     // Rare: lanes without a redo fold block 1 first (a[] is then free), then the warp re-reads it for the others,
     // then releases.
     if (first) block_first(a, cmax, M, L);
     else if (!redo) block_fold(a, cmax, M, L);
-    block_redo(taddr + (uint32_t)N, bias + N, dot2, redo, a, M, L);
+    const float2 r = block_redo(taddr + (uint32_t)N, dot2, redo, M, L);
+    M = r.x;
+    L = r.y;
     tmem_fence_before();
     mbar_arrive(acc_empty);
   } else {
@@ -328,9 +323,45 @@ __device__ __forceinline__ void lse_tile128(uint32_t taddr, const float* bias, f
   }
 }
 
-// Instruction descriptor, kind::f16: D F32, A and B FP16, both K-major, N = TC_BN, M = 128.
+// Instruction descriptors, kind::f16: D F32, A and B FP16 (kIdesc) or both BF16 (kIdescBf16), K-major,
+// N = TC_BN, M = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                             ((uint32_t)(TC_BM >> 4) << 24);
+constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+                                ((uint32_t)(TC_BM >> 4) << 24);
+
+// Shared-memory descriptor of a K-major operand without swizzling: 8-row x 16-byte core matrices, `lbo` bytes
+// between the two core matrices of a K = 16 (BF16) slice, `sbo` bytes between 8-row groups.
+__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;                           // descriptor version (sm_100); layout 0: no swizzle
+  return d;
+}
+
+// The column bias enters the accumulator through one more MMA per tile, K = 16 in BF16: A is a constant tile whose
+// rows are [1, 1, 1, 0, ...], B holds for each column j the bias_j / dot2 split into three BF16 parts
+// (8 + 8 + 8 significant bits, FP32-level), so acc_ij = x_i.y_j (scaled) + bias_j / dot2 and the epilogue needs no
+// per-column term. Plain layout: core matrix (row group g, K half h) at g * 256 + h * 128, row r of the group at
+// r * 16, element k of the half at 2 k.
+constexpr uint32_t kBiasLbo = 128, kBiasSbo = 256;
+constexpr int kBiasABytes = TC_BM * 32;      // 128 rows x 16 BF16
+constexpr int kBiasBBytes = TC_BN * 32;      // 256 rows x 16 BF16
+
+__device__ __forceinline__ uint32_t bias_row_offset(int row) { return (uint32_t)((row >> 3) * 256 + (row & 7) * 16); }
+
+// x -> three BF16 parts whose sum is x to FP32 precision; -inf (a column past m) -> (-inf, 0, 0).
+__device__ __forceinline__ uint2 bias_split(float x) {
+  const __nv_bfloat16 h1 = __float2bfloat16_rn(x);
+  if (!(x > -INFINITY)) return make_uint2((uint32_t)__bfloat16_as_ushort(h1), 0u);
+  const float r1 = x - __bfloat162float(h1);
+  const __nv_bfloat16 h2 = __float2bfloat16_rn(r1);
+  const __nv_bfloat16 h3 = __float2bfloat16_rn(r1 - __bfloat162float(h2));
+  return make_uint2((uint32_t)__bfloat16_as_ushort(h1) | ((uint32_t)__bfloat16_as_ushort(h2) << 16),
+                    (uint32_t)__bfloat16_as_ushort(h3));
+}
 
 // ------------------------------------------------------------------------------------------------------------
 // The kernel
@@ -342,11 +373,12 @@ struct TcCfg {
   static constexpr int B_BYTES = NKB * TC_BN * 128;      // one column tile
   static constexpr int NS = NKB == 1 ? 4 : 2;            // column-tile stages
   static constexpr int OFF_B = 2 * A_BYTES;
-  static constexpr int OFF_BIAS = OFF_B + NS * B_BYTES;
-  static constexpr int OFF_BAR = OFF_BIAS + TC_NBIAS * TC_BN * 4;
-  // barriers: full[NS], empty[NS], a_full[2], a_empty[2], acc_full[NACC], acc_empty[NACC], bias_full[NB],
-  // bias_empty[NB], drain[1]
-  static constexpr int NBAR = 2 * NS + 4 + 2 * TC_NACC + 2 * TC_NBIAS + 1;
+  static constexpr int OFF_BIAS_A = OFF_B + NS * B_BYTES;                 // constant BF16 tile [1, 1, 1, 0 ...]
+  static constexpr int OFF_BIAS_B = OFF_BIAS_A + kBiasABytes;             // TC_NBB column-bias operand slots
+  static constexpr int OFF_BAR = OFF_BIAS_B + TC_NBB * kBiasBBytes;
+  // barriers: full[NS], empty[NS], a_full[2], a_empty[2], acc_full[NACC], acc_empty[NACC], bias_full[NBB],
+  // bias_empty[NBB], drain[1]
+  static constexpr int NBAR = 2 * NS + 4 + 2 * TC_NACC + 2 * TC_NBB + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;     // + alignment slack for the 1024-byte aligned base
 };
@@ -377,12 +409,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* acc_full = a_empty + 2;
   uint64_t* acc_empty = acc_full + TC_NACC;
   uint64_t* bias_full = acc_empty + TC_NACC;
-  uint64_t* bias_empty = bias_full + TC_NBIAS;
-  uint64_t* drain = bias_empty + TC_NBIAS;
+  uint64_t* bias_empty = bias_full + TC_NBB;
+  uint64_t* drain = bias_empty + TC_NBB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   int* s_last = reinterpret_cast<int*>(smem + C::OFF_MISC + 16);     // [2], one per epilogue warpgroup
-  float* bias_ring = reinterpret_cast<float*>(smem + C::OFF_BIAS);
 
   if (blockDim.x != TC_THREADS) {
     if (threadIdx.x == 0) atomicOr(p.error_word, (int)kErrBadLaunch);
@@ -392,10 +423,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int s = 0; s < C::NS; ++s) { mbar_init(&full_b[s], 1); mbar_init(&empty_b[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&a_full[b], 1); mbar_init(&a_empty[b], 1); }
     for (int b = 0; b < TC_NACC; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 256); }
-    for (int s = 0; s < TC_NBIAS; ++s) { mbar_init(&bias_full[s], 32); mbar_init(&bias_empty[s], 256); }
+    for (int s = 0; s < TC_NBB; ++s) { mbar_init(&bias_full[s], 32); mbar_init(&bias_empty[s], 1); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  {
+    // Bias operands: A rows [1, 1, 1, 0 ... 0] (BF16 1.0 = 0x3F80), B slots zero (the bias warp fills K 0..2 of
+    // each row per tile; K 3..15 must stay finite). Written through the generic proxy, read by the tensor core.
+    uint4* ba = reinterpret_cast<uint4*>(smem + C::OFF_BIAS_A);
+    for (int q = threadIdx.x; q < kBiasABytes / 16; q += blockDim.x) {
+      const bool k_lo = ((q >> 3) & 1) == 0;          // 16-byte row chunk of K half 0 (elements 0..7)
+      ba[q] = k_lo ? make_uint4(0x3F803F80u, 0x3F80u, 0u, 0u) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    uint4* bb = reinterpret_cast<uint4*>(smem + C::OFF_BIAS_B);
+    for (int q = threadIdx.x; q < TC_NBB * kBiasBBytes / 16; q += blockDim.x) bb[q] = make_uint4(0u, 0u, 0u, 0u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == TC_MMA_WARP) {
@@ -466,11 +509,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else if (warp == TC_BIAS_WARP) {
-    // ---------------------------------------------------------------- column bias, (gh / eps + log b) log2(e)
-    // All loads of a tile are issued before any shared-memory store (restrict-qualified, read-only path), so a
-    // tile costs one L2 round trip; the 4-slot ring lets this warp run ahead of the epilogue.
+    // ---------------------------------------------------------------- column bias operand
+    // bias_j = (gh_j / eps + log b_j) log2(e), stored as bias_j / dot2 in three BF16 parts (K = 0, 1, 2 of row j
+    // of the slot's B operand). All loads of a tile are issued before waiting for the slot, so a tile costs one
+    // L2 round trip, overlapped with the MMAs of the tile before.
     const float* __restrict__ ghp = p.gh;
     const float* __restrict__ lbp = p.log_b;
+    const float inv_dot2 = 1.0f / p.dot2;
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the previous grid (which may write gh) is complete
     int T = 0;
     bool ok = true;
@@ -494,12 +539,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         g[q] = j < p.m ? __ldcg(ghp + j) : 0.f;
         l[q] = j < p.m ? __ldg(lbp + j) : -INFINITY;
       }
-      const int bslot = T % TC_NBIAS;
-      ok = mbar_wait(&bias_empty[bslot], ((T / TC_NBIAS) & 1) ^ 1, abort_flag, p.error_word);
+      const int bslot = T % TC_NBB;
+      ok = mbar_wait(&bias_empty[bslot], ((T / TC_NBB) & 1) ^ 1, abort_flag, p.error_word);
       if (!ok) break;
-      float* bias = bias_ring + bslot * TC_BN;
+      uint8_t* bb = smem + C::OFF_BIAS_B + bslot * kBiasBBytes;
 #pragma unroll
-      for (int q = 0; q < TC_BN / 32; ++q) bias[q * 32 + lane] = fmaf(l[q], p.lb2, g[q] * p.gh2);
+      for (int q = 0; q < TC_BN / 32; ++q) {
+        const float x = fmaf(l[q], p.lb2, g[q] * p.gh2) * inv_dot2;
+        *reinterpret_cast<uint2*>(bb + bias_row_offset(q * 32 + lane)) =
+            bias_split(fminf(fmaxf(x, -1e36f), 1e36f) + (x == -INFINITY ? -INFINITY : 0.f));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&bias_full[bslot]);
     }
   } else if (warp == TC_MMA_WARP) {
@@ -509,6 +559,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       bool ok = true;
       const uint32_t a_base = smem_u32(smem);
       const uint32_t b_base = smem_u32(smem + C::OFF_B);
+      const uint32_t bias_a = smem_u32(smem + C::OFF_BIAS_A);
+      const uint32_t bias_b = smem_u32(smem + C::OFF_BIAS_B);
       for (long long u = u_begin; u < u_end && ok; ++seg) {
         const int r = (int)(u / sk.nct);
         const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
@@ -540,6 +592,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
           umma_commit(&empty_b[stage]);
+          // last, the column bias (it is the only input that waits for the previous grid)
+          const int bslot = T % TC_NBB;
+          ok = mbar_wait(&bias_full[bslot], (T / TC_NBB) & 1, abort_flag, p.error_word);
+          if (!ok) break;
+          tmem_fence_after();
+          umma_f16(d_tmem, plain_desc(bias_a, kBiasLbo, kBiasSbo),
+                   plain_desc(bias_b + (uint32_t)(bslot * kBiasBBytes), kBiasLbo, kBiasSbo), kIdescBf16, 1u);
+          umma_commit(&bias_empty[bslot]);
           umma_commit(&acc_full[acc]);
         }
         if (ok) umma_commit(&a_empty[a_slot]);
@@ -568,13 +628,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!ok) continue;
         const int acc = T % TC_NACC;
         ok = mbar_wait(&acc_full[acc], (T / TC_NACC) & 1, abort_flag, p.error_word);
-        const int bslot = T % TC_NBIAS;
-        if (ok) ok = mbar_wait(&bias_full[bslot], (T / TC_NBIAS) & 1, abort_flag, p.error_word);
         if (!ok) continue;
         tmem_fence_after();
-        lse_tile128(lane_base + (uint32_t)(acc * TC_BN), bias_ring + bslot * TC_BN + wg * (TC_BN / 2), dot2, M, L,
-                    &acc_empty[acc]);
-        mbar_arrive(&bias_empty[bslot]);
+        lse_tile128(lane_base + (uint32_t)(acc * TC_BN), dot2, M, L, &acc_empty[acc]);
       }
       // Segment done: this warpgroup's partial for row tile r, then one arrival on the row tile's counter.
       const long long first_u = (long long)r * sk.nct;
