@@ -416,9 +416,10 @@ def run_ours(args, rank, world, dev):
             "frac": round(tflops / bf16, 4), "traffic": traffic, "peak_source": peak_src,
             "kernel": f"half-step ({path})", "launch_ms": round(launch_ms, 5),
             "sfu": {"achieved_exp_per_s": sfu_rate, "peak_exp_per_s": sfu_peak, "frac": round(sfu_rate / sfu_peak, 4),
-                    "clock_mhz": mhz},
-            "ffma": {"achieved_tflops": round(tflops, 2), "peak_tflops": round(ffma_peak, 2),
-                     "frac": round(tflops / ffma_peak, 4)}}
+                    "clock_mhz": mhz}}
+    if path == "ffma":
+        roof["ffma"] = {"achieved_tflops": round(tflops, 2), "peak_tflops": round(ffma_peak, 2),
+                        "frac": round(tflops / ffma_peak, 4)}
 
     # End to end through the public API: host arrays in, potentials out, K iterations.
     e2e = None
