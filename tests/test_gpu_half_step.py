@@ -166,6 +166,34 @@ def test_workspace_is_left_ready_and_results_are_deterministic(path):
     assert _capi.device_error_flags() == 0
 
 
+def _half_step_f64_on_gpu(x, xsq, off, y, gh, log_b, eps, kappa):
+    """The half-step (sinkhorn.py:108-119) in float64 with torch on the GPU, for sizes the CPU oracle is slow at."""
+    t = lambda a: torch.as_tensor(np.asarray(a, dtype=np.float64), device="cuda")
+    X, Y = t(x), t(y)
+    z = (2.0 * X @ Y.T + t(gh)[None, :]) / eps + t(log_b)[None, :]
+    lse = torch.logsumexp(z, dim=1)
+    off = np.zeros(len(x)) if off is None else off
+    return (kappa * (t(xsq) + eps * t(off) - eps * lse) - t(xsq)).cpu().numpy()
+
+
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
+def test_calls_of_different_shapes_share_a_workspace(path):
+    """The f and g half-steps of a solve share one workspace although their row-tile counts differ (here 64 and
+    70 tiles, on either side of a 64-counter block): every row of every output is checked, twice round."""
+    n, m, d, eps = 8142, 8930, 16, 0.1
+    x, xsq, off, y, gh, lb = problem(n, m, d, 3, eps)
+    ysq = (y * y).sum(1)
+    la = np.full(n, -np.log(n))
+    ws = _capi.new_workspace(max(_capi.workspace_size(n, m, d, path), _capi.workspace_size(m, n, d, path)), "cuda")
+    for _ in range(2):
+        fh = gpu_half_step(x, xsq, off, y, gh, lb, eps, 0.9, ws=ws, path=path)
+        ref = _half_step_f64_on_gpu(x, xsq, off, y, gh, lb, eps, 0.9)
+        assert np.abs(fh - ref).max() / eps <= HS_TOL
+        gh = gpu_half_step(y, ysq, None, x, fh, la, eps, 1.0, ws=ws, path=path)
+        ref = _half_step_f64_on_gpu(y, ysq, None, x, fh, la, eps, 1.0)
+        assert np.abs(gh - ref).max() / eps <= HS_TOL
+
+
 def test_argument_errors_are_reported_not_launched():
     x, xsq, off, y, gh, lb = problem(10, 20, 4, 2, 0.1)
     xT, ldx = _capi._pad_ld(_dev(x.T))

@@ -62,13 +62,29 @@ int current_device() {
   return dev;
 }
 
-// Carve the workspace: [counters (nrt ints, 256-byte padded)][partials].
+// Counters region at the start of a workspace of ws_bytes: one int per KB of workspace. No call can have more row
+// tiles than that (each row tile needs at least one 1 KB block of partials), and the size depends on ws_bytes
+// only, so every call sharing a workspace (the f and g half-steps of a solve, of different shapes) puts its partials
+// at the same offset, past every call's counters: a call's partials never overwrite another call's counters, and
+// counters that calls share are zero between launches (every launch re-arms the counters it uses).
+size_t counter_region(size_t ws_bytes) {
+  return ((ws_bytes / 1024) * sizeof(int) + kCounterRegion - 1) / kCounterRegion * kCounterRegion;
+}
+
+// Smallest workspace that holds `partial_bytes` of partials past its counter region, for nrt row tiles.
+size_t workspace_bytes(size_t partial_bytes, int nrt) {
+  size_t w = partial_bytes + counter_bytes(nrt);
+  while (counter_region(w) + partial_bytes > w || counter_region(w) < counter_bytes(nrt)) w += kCounterRegion;
+  return w;
+}
+
 int bind_workspace(StreamK& sk, size_t partial_bytes, void* ws, size_t ws_bytes) {
-  const size_t need = counter_bytes(sk.nrt) + partial_bytes;
-  if (ws == nullptr || ws_bytes < need) return TRNOPT_ERR_WORKSPACE;
+  const size_t region = counter_region(ws_bytes);
+  if (ws == nullptr || counter_bytes(sk.nrt) > region || region + partial_bytes > ws_bytes)
+    return TRNOPT_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return TRNOPT_ERR_ALIGNMENT;
   sk.counters = reinterpret_cast<int*>(ws);
-  sk.partials = reinterpret_cast<float2*>(reinterpret_cast<char*>(ws) + counter_bytes(sk.nrt));
+  sk.partials = reinterpret_cast<float2*>(reinterpret_cast<char*>(ws) + region);
   return TRNOPT_OK;
 }
 
@@ -168,7 +184,7 @@ size_t trnopt_workspace_size(int rows, int m, int d, int path) {
   } else {
     return 0;
   }
-  return counter_bytes(sk.nrt) + partial;
+  return workspace_bytes(partial, sk.nrt);
 }
 
 int trnopt_workspace_init(void* workspace, size_t ws_bytes, void* stream) {

@@ -3,8 +3,8 @@
 // Some callers of this library have no way to call cudaMalloc: code running inside a CUDA graph that is being
 // captured by someone else, plugin hosts that hand out only the input and output buffers, and allocators that
 // forbid allocations after start-up (an arena sized once at launch). For them this entry point takes the same
-// inputs and outputs as trnopt_half_step_tc and keeps its scratch (the per-row partial maxima/sums and the
-// per-row-tile arrival counters) in a fixed array compiled into the library instead of a caller workspace.
+// inputs and outputs as trnopt_half_step_tc and keeps its scratch (the per-row-tile arrival counters, then the
+// per-row partial maxima/sums) in a fixed array compiled into the library instead of a caller workspace.
 //
 // Limits and sharing:
 //   * The array is kStaticScratchBytes (4 MiB) per GPU, held from the moment the library is loaded on that GPU until

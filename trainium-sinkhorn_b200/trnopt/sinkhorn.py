@@ -118,11 +118,10 @@ def _exchange(how: str, path: str) -> str:
     return how
 
 
-def _scale_exp(P: np.ndarray) -> int:
-    """Power-of-two exponent that brings the largest |coordinate| into (2^13, 2^14] for the FP16 split of the TC
+def _scale_exp(mx: float) -> int:
+    """Power-of-two exponent that brings the largest |coordinate| mx into (2^13, 2^14] for the FP16 split of the TC
     path: high enough that the low halves of typical coordinates stay normal FP16 numbers (11 significant bits;
     subnormals keep only absolute precision 2^-24), low enough that hi + lo stays below FP16's 65504."""
-    mx = float(np.abs(P).max()) if P.size else 0.0
     return 0 if mx == 0.0 else 14 - int(np.ceil(np.log2(mx)))
 
 
@@ -161,36 +160,34 @@ class _Cloud:
     """One point cloud on this rank's GPU, padded to a whole number of row tiles per shard.
 
     xT (d, npad) float32 transposed points (the layout of the reference's NKI path, sinkhorn.py:159-165), sq the
-    squared norms (float64 on the host, then cast, as sinkhorn.py:149), log_w with PAD_LOG_WEIGHT on padding, w the
-    weights (padding exactly 0), off the row offsets log(target / reference) (0 on padding)."""
+    squared norms (float64, then cast, as sinkhorn.py:149; sq64 keeps the float64 values on the device), log_w
+    with PAD_LOG_WEIGHT on padding, w the weights (padding exactly 0), off the row offsets log(target / reference)
+    (0 on padding). `pts` is an (n, d) float64 tensor already on the device (or a host array, uploaded here): the
+    padding, transpose, norms and weights are all formed on the device."""
 
-    def __init__(self, pts: np.ndarray, log_w: np.ndarray, shards: int, dev: torch.device, off=None):
+    def __init__(self, pts, log_w: np.ndarray, shards: int, dev: torch.device, off=None):
+        if not isinstance(pts, torch.Tensor):
+            pts = torch.as_tensor(np.ascontiguousarray(pts, dtype=np.float64)).to(dev)
         n, d = pts.shape
         unit = ROW_TILE * shards
         npad = -(-n // unit) * unit
         self.n, self.npad, self.d, self.shards = n, npad, d, shards
-        # Points go up once as (n, d) float32; padding and the transpose happen on the device.
-        p32 = torch.from_numpy(np.ascontiguousarray(pts, dtype=np.float32))
-        if dev.type == "cuda":
-            p32 = p32.pin_memory()
         xT = torch.zeros((d, npad), dtype=torch.float32, device=dev)
-        xT[:, :n] = p32.to(dev, non_blocking=True).T
+        xT[:, :n] = pts.T
         self.xT = xT
-        sq = np.zeros(npad)
-        sq[:n] = (pts * pts).sum(axis=1)                   # float64 on the host, then cast (sinkhorn.py:149)
-        self.sq64 = sq
-        vec = np.zeros((4, npad))
-        vec[0] = sq
+        vec = torch.zeros((4, npad), dtype=torch.float64, device=dev)
+        vec[0, :n] = (pts * pts).sum(dim=1)                  # float64, then cast (sinkhorn.py:149)
         vec[1] = PAD_LOG_WEIGHT
-        vec[1, :n] = log_w
-        vec[2] = np.exp(vec[1])
+        vec[1, :n] = torch.as_tensor(np.asarray(log_w, dtype=np.float64)).to(dev)
+        vec[2] = torch.exp(vec[1])
         if off is not None:
-            vec[3, :n] = off
-        v32 = torch.from_numpy(vec.astype(np.float32)).to(dev)
+            vec[3, :n] = torch.as_tensor(np.asarray(off, dtype=np.float64)).to(dev)
+        self.sq64 = vec[0]
+        v32 = vec.to(torch.float32)
         self.sq, self.log_w, self.w, self.off = v32[0], v32[1], v32[2], v32[3]
         self.zero = torch.zeros(npad, dtype=torch.float32, device=dev)
-        self.h2d_bytes = 4 * (n * d + 4 * npad)
-        self.sexp = _scale_exp(pts)
+        self.h2d_bytes = 8 * (n * d + n + (n if off is not None else 0))
+        self.sexp = _scale_exp(float(pts.abs().max()) if n else 0.0)
         self.packed = None
 
     def pack(self) -> None:
@@ -344,11 +341,17 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
             center, scale = normalization(x, y, how=opts.normalize if isinstance(opts.normalize, str) else "mean")
     else:
         center, scale = np.zeros(x.shape[1]), 1.0
-    xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
-    shift = np.concatenate([xs, ys]).mean(axis=0)          # internal frame: joint mean at the origin
-    xi, yi = xs - shift, ys - shift
 
     with torch.cuda.device(dev):
+        # One float64 upload per cloud; the normalisation (sinkhorn.py:268-269) and the internal frame (joint mean at
+        # the origin) in float64 on the device.
+        xd = torch.as_tensor(x).to(dev)
+        yd = torch.as_tensor(y).to(dev)
+        c = torch.as_tensor(np.asarray(center, dtype=np.float64)).to(dev)
+        r = float(np.sqrt(scale))
+        xs, ys = (xd - c) / r, (yd - c) / r
+        shift = torch.cat([xs, ys]).mean(dim=0)
+        xi, yi = xs - shift, ys - shift
         X = _Cloud(xi, log_a, shards, dev, off_x)
         Y = _Cloud(yi, log_b, shards, dev, off_y)
         path = _resolve_path(opts.cuda_path, X.d)
@@ -369,8 +372,9 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
 
         # The reference starts from gh = 0 in its frame, i.e. g = |ys|^2; in the internal frame that is
         # gh = |ys|^2 - |yi|^2 (exactly the same iteration).
-        gh0 = np.zeros(Y.npad)
-        gh0[:Y.n] = (ys * ys).sum(1) - (yi * yi).sum(1)
+        gh0 = torch.zeros(Y.npad, dtype=torch.float64, device=dev)
+        gh0[:Y.n] = (ys * ys).sum(dim=1) - (yi * yi).sum(dim=1)
+        del xd, yd, xs, ys, xi, yi
         # Ping-pong potentials: before iteration i the shifted g is G[i % 2]; fh has one buffer.
         peer = None
         if shards > 1 and _exchange(opts.cuda_exchange, path) == "peer":
@@ -430,13 +434,13 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
                 converged = True
                 break
         gh = G[it % 2]
-        f = fh[:X.n].to(torch.float64).cpu().numpy() + X.sq64[:X.n]
-        g = gh[:Y.n].to(torch.float64).cpu().numpy() + Y.sq64[:Y.n]
+        f = (fh[:X.n].to(torch.float64) + X.sq64[:X.n]).cpu().numpy()
+        g = (gh[:Y.n].to(torch.float64) + Y.sq64[:Y.n]).cpu().numpy()
         row_mass = col_mass = None
         if not balanced:
             # The plan's marginals from one balanced (kappa = 1, no offset) update each way (sinkhorn.py:381-389).
-            fb = step(X, Y, gh, opts.eps, 1.0, use_off=False)[:X.n].to(torch.float64).cpu().numpy() + X.sq64[:X.n]
-            gb = step(Y, X, fh, opts.eps, 1.0, use_off=False)[:Y.n].to(torch.float64).cpu().numpy() + Y.sq64[:Y.n]
+            fb = (step(X, Y, gh, opts.eps, 1.0, use_off=False)[:X.n].to(torch.float64) + X.sq64[:X.n]).cpu().numpy()
+            gb = (step(Y, X, fh, opts.eps, 1.0, use_off=False)[:Y.n].to(torch.float64) + Y.sq64[:Y.n]).cpu().numpy()
             row_mass = np.exp(log_a + (f - fb) / opts.eps)
             col_mass = np.exp(log_b + (g - gb) / opts.eps)
         flags = _capi.device_error_flags()
