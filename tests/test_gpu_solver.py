@@ -136,3 +136,19 @@ def test_cfg2_full_size_column_sums():
     mx = logP.max(0)
     col_sum = np.exp(mx) * np.exp(logP - mx).sum(0)
     np.testing.assert_allclose(col_sum * len(y), 1.0, rtol=1e-4)
+
+
+def test_wot_transport_map_full_cfg3_masses():
+    """Config 3 at full size (7,355 x 8,962, d 30; 58 and 71 row tiles, so the two half-steps have different
+    workspace shapes): the plan's row and column masses are finite and positive and both count the same total
+    mass (a size-independent property of any plan), after each of wot's growth iterations."""
+    from trnopt.singlecell import wot_transport_map
+    x0, x1, growth = synthetic.cfg3()
+    tm = wot_transport_map(x0, x1, growth, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8,
+                           opts=SinkhornOptions(backend=BE))
+    r = tm.result
+    for v in (r.row_mass, r.col_mass, r.f, r.g):
+        assert np.all(np.isfinite(v))
+    assert np.all(r.row_mass > 0) and np.all(r.col_mass > 0)
+    assert abs(r.row_mass.sum() / r.col_mass.sum() - 1) < 1e-3
+    assert len(tm.learned_growth) == 3 and all(np.all(np.isfinite(g)) for g in tm.learned_growth)
