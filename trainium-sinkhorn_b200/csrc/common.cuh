@@ -96,21 +96,33 @@ __device__ __forceinline__ void lse_merge(float& M, float& l, float M2, float l2
 }
 
 // Finish one row: merge nparts partials (M, l) in double precision and apply the kappa / off epilogue
-// (reference src/trnopt/sinkhorn.py:119, src/trnopt/nki_sinkhorn.py:212-225).
+// (reference src/trnopt/sinkhorn.py:119, src/trnopt/nki_sinkhorn.py:212-225). The loads of the first kRegParts
+// partials and of the row's own inputs are issued together (one memory round trip for the usual 2-8 partials);
+// the merge order is the partials' order either way.
 __device__ inline float finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride) {
+  constexpr int kRegParts = 8;
+  const float xsq = p.mode == 0 ? __ldg(p.xsq + row) : 0.f;
+  const float off = (p.mode == 0 && p.off) ? __ldg(p.off + row) : 0.f;
+  float2 v[kRegParts];
+#pragma unroll
+  for (int s = 0; s < kRegParts; ++s)
+    v[s] = s < nparts ? __ldcg(&parts[(size_t)s * stride]) : make_float2(kMaxFloor, 0.f);
   float M = kMaxFloor;
-  for (int s = 0; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
+#pragma unroll
+  for (int s = 0; s < kRegParts; ++s) M = fmaxf(M, v[s].x);
+  for (int s = kRegParts; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
   double l = 0.0;
-  for (int s = 0; s < nparts; ++s) {
-    float2 v = __ldcg(&parts[(size_t)s * stride]);
-    if (v.y > 0.f) l += (double)v.y * exp2((double)v.x - (double)M);
+#pragma unroll
+  for (int s = 0; s < kRegParts; ++s)
+    if (v[s].y > 0.f) l += (double)v[s].y * exp2((double)v[s].x - (double)M);
+  for (int s = kRegParts; s < nparts; ++s) {
+    const float2 w = __ldcg(&parts[(size_t)s * stride]);
+    if (w.y > 0.f) l += (double)w.y * exp2((double)w.x - (double)M);
   }
   double lse = ((double)M + log2(l)) * kLn2;
   double res;
   if (p.mode == 0) {
-    double xsq = (double)p.xsq[row];
-    double off = p.off ? (double)p.off[row] : 0.0;
-    res = p.kappa * (xsq + p.eps * off - p.eps * lse) - xsq;
+    res = p.kappa * ((double)xsq + p.eps * (double)off - p.eps * lse) - (double)xsq;
   } else {
     res = lse;
   }
