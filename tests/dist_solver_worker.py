@@ -17,8 +17,47 @@ import torch.distributed as dist  # noqa: E402
 from trnopt import Backend, SinkhornOptions, sinkhorn  # noqa: E402
 
 
+def peer_timeout(out):
+    """Rank 1 joins the peer region and then skips its half-steps (a host decision between steps, none of its kernels
+    in flight); rank 0's run waits for rank 1's rows, gives up after the kernels' time limit and reports error bit 8
+    (another GPU did not publish) through trnopt_device_error_flags."""
+    from trnopt import _capi, _comm
+    import trnopt.sinkhorn  # noqa: F401
+    S = sys.modules["trnopt.sinkhorn"]
+    rank = dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(0)
+    x, y = rng.uniform(size=(600, 16)), rng.uniform(size=(500, 16))
+    X = S._Cloud(x, np.full(600, -np.log(600)), 2, dev)
+    Y = S._Cloud(y, np.full(500, -np.log(500)), 2, dev)
+    X.pack()
+    Y.pack()
+    ws = S._workspace(X, Y, 2, dev, "tc")
+    reg = _comm.PeerRegion(4 * (X.npad + 2 * Y.npad))
+    fh = reg.tensor(0, X.npad)
+    G = [reg.tensor(4 * X.npad, Y.npad), reg.tensor(4 * (X.npad + Y.npad), Y.npad)]
+    G[0].zero_()
+    fh.zero_()
+    reg.arrive()
+    flags = -1
+    if rank == 0:
+        _capi.sinkhorn_run_sharded(reg.comm, X.packed, X.sq, None, X.log_w, X.npad, X.sexp, Y.packed, Y.sq, None,
+                                   Y.log_w, Y.npad, Y.sexp, X.d, G[0], G[1], fh, 0, 1, 0.1, 1.0, 1.0, ws)
+        torch.cuda.synchronize()
+        flags = _capi.device_error_flags()
+        np.savez(out, flags=flags)
+    dist.barrier()
+
+
 def main():
     out = sys.argv[1]
+    if len(sys.argv) > 2 and sys.argv[2] == "peer_timeout":
+        local = int(os.environ["LOCAL_RANK"])
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=60))
+        peer_timeout(out)
+        dist.destroy_process_group()
+        return
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=60))

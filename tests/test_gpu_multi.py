@@ -1,4 +1,4 @@
-"""Rows of every half-step split across 2 GPUs (one process per GPU; the new potential reaches every GPU either by
+"""Rows of every half-step split across 2 or 4 GPUs (one process per GPU; the new potential reaches every GPU either by
 peer stores from the half-step kernels or by an NCCL all-gather) give the single-GPU answer: the counterpart of the
 reference's two-cores-match-one test (tests/test_sinkhorn.py:174-183)."""
 import os
@@ -14,13 +14,15 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpus_match_one(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_gpus_match_one(tmp_path, world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from trnopt import Backend, SinkhornOptions, sinkhorn
-    out = tmp_path / "two.npz"
+    out = tmp_path / f"world{world}.npz"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "420", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29600 + os.getpid() % 200}",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29600 + world + os.getpid() % 200}",
            str(ROOT / "tests" / "dist_solver_worker.py"), str(out)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
@@ -45,3 +47,18 @@ def test_two_gpus_match_one(tmp_path):
     # the two exchanges move the same float32 rows: identical results
     for k in ("f", "g", "fu", "gu", "fb", "gb"):
         np.testing.assert_array_equal(z[f"peer_{k}"], z[f"nccl_{k}"], err_msg=k)
+
+
+def test_peer_wait_gives_up_when_a_gpu_stops_publishing(tmp_path):
+    """Failure detection on the peer exchange without a GPU fault: one rank stops between steps; the other rank's
+    half-step waits for its rows, gives up after the kernels' time limit (4 s) and the host reads error bit 8."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "timeout.npz"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29700 + os.getpid() % 200}",
+           str(ROOT / "tests" / "dist_solver_worker.py"), str(out), "peer_timeout"]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert int(np.load(out)["flags"]) & 8
