@@ -316,6 +316,48 @@ def pull_back(x0, x1, f, g, eps, center, scale, log_v1, chunk: int = 1024):
     return out - logsumexp(out)
 
 
+def local_pca_coords(X0, X1, n_components: int = 30, random_state: int = 58951):
+    """singlecell.py:30-43: PCA of the centred stacked expression fitted on the transpose, components scaled by the
+    singular values. The reference calls scikit-learn's PCA (pinned 1.7.2, uv.lock:3252-3253); this restates the
+    algorithm its `auto` policy runs (sklearn/decomposition/_pca.py _fit_full / _fit_truncated,
+    sklearn/utils/extmath.py _randomized_svd / _randomized_range_finder / svd_flip) with NumPy and SciPy."""
+    from scipy import linalg
+    x = np.vstack([np.asarray(X0), np.asarray(X1)]).astype(np.float64)
+    x = x - x.mean(axis=0)
+    k = min(n_components, x.shape[0])
+    A = x.T
+    n_samples, n_features = A.shape
+    mean = A.mean(axis=0)
+    if n_features <= 1000 and n_samples >= 10 * n_features:
+        C = A.T @ A - n_samples * np.outer(mean, mean)
+        C /= n_samples - 1
+        ev, vecs = linalg.eigh(C)
+        ev, vecs = ev[::-1].copy(), vecs[:, ::-1].copy()
+        ev[ev < 0] = 0.0
+        S, Vt = np.sqrt(ev * (n_samples - 1)), vecs.T
+    elif max(A.shape) <= 500 or not (1 <= k < 0.8 * min(A.shape)):
+        _, S, Vt = linalg.svd(A - mean, full_matrices=False)
+    else:
+        M = A - mean
+        rs = np.random.RandomState(random_state)
+        n_random, n_iter = k + 10, (7 if k < 0.1 * min(M.shape) else 4)
+        transpose = M.shape[0] < M.shape[1]
+        if transpose:
+            M = M.T
+        Q = rs.normal(size=(M.shape[1], n_random))
+        for _ in range(n_iter):
+            Q, _ = linalg.lu(M @ Q, permute_l=True)
+            Q, _ = linalg.lu(M.T @ Q, permute_l=True)
+        Q, _ = linalg.qr(M @ Q, mode="economic")
+        Uhat, s, Vb = linalg.svd(Q.T @ M, full_matrices=False)
+        U = Q @ Uhat
+        S, Vt = (s[:k], U[:, :k].T) if transpose else (s[:k], Vb[:k])
+    idx = np.argmax(np.abs(Vt), axis=1)
+    Vt = Vt * np.sign(Vt[np.arange(Vt.shape[0]), idx])[:, None]
+    comp = Vt[:k].T * S[:k][None, :]
+    return comp[:len(X0)], comp[len(X0):]
+
+
 # --------------------------------------------------------------------------------------------------------------
 # wot formulation (singlecell.py:46-86)
 # --------------------------------------------------------------------------------------------------------------

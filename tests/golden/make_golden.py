@@ -16,6 +16,9 @@ Files:
                         and the fp64 plan's row / column sums
   normalization.npz     normalization() scales (mean and median, odd and even n m, config 3's full pair)
   wot_small.npz         wot_transport_map() on a reduced config-3 pair (fp64, 3 growth iterations)
+  pca_cases.npz         local_pca_coords (singlecell.py:30-43) on seeded synthetic expression, one shape per
+                        solver sklearn's PCA picks: randomized (700 cells x 1200 genes and 900 x 600), full
+                        (180 x 300), covariance_eigh (120 x 2400)
   plan_cases.npz        plan quantities from wot_small's potentials: rows of transport_plan (sinkhorn.py:397-403),
                         the plan's row / column sums, masses_from_potentials
                         (examples/sinkhorn_libs_compare.py:43-56) and the ancestor pull-back
@@ -190,6 +193,16 @@ def _example(name):
     return mod
 
 
+def pca_cases():
+    from trnopt.singlecell import local_pca_coords as ref_pca
+    out = {}
+    for tag, (c0, c1, genes, seed) in synthetic.PCA_CASES.items():
+        e0, e1 = synthetic.expression(c0, c1, genes, seed)
+        p0, p1 = ref_pca(e0, e1, 30)
+        out[f"{tag}_p0"], out[f"{tag}_p1"] = p0, p1
+    np.savez_compressed(HERE / "pca_cases.npz", **out)
+
+
 def plan_cases():
     import tempfile
     z = np.load(HERE / "wot_small.npz")
@@ -224,7 +237,7 @@ def plan_cases():
 
 if __name__ == "__main__":
     which = sys.argv[1:] or ["half_step_kat", "row_lse_kat", "solver_cases", "cfg1", "normalization", "wot_small",
-                             "plan_cases"]
+                             "plan_cases", "pca_cases"]
     for w in which:
         print("generating", w, flush=True)
         globals()[w]()

@@ -132,3 +132,17 @@ def test_plan_marginals_at_cfg2_size():
     # after the g update the column sums are b up to float64 evaluation of fp32 potentials
     assert np.abs(cols * len(y) - 1).max() < 2e-3
     assert np.abs(rows * len(x) - 1).sum() / len(x) < 1e-5 * 50
+
+
+@pytest.mark.parametrize("tag", list(synthetic.PCA_CASES))
+def test_local_pca_coords_match_reference(golden, tag):
+    """GPU local PCA (wot's per-pair embedding) against the reference's local_pca_coords on the same seeded
+    expression, for each solver sklearn's PCA picks (randomized, transposed randomized, full, covariance-eigh)."""
+    from trnopt.singlecell import local_pca_coords
+    z = golden("pca_cases.npz")
+    c0, c1, genes, seed = synthetic.PCA_CASES[tag]
+    e0, e1 = synthetic.expression(c0, c1, genes, seed)
+    p0, p1 = local_pca_coords(e0, e1, 30)
+    scale = np.abs(z[f"{tag}_p0"]).max()
+    np.testing.assert_allclose(p0, z[f"{tag}_p0"], rtol=0, atol=1e-8 * scale)
+    np.testing.assert_allclose(p1, z[f"{tag}_p1"], rtol=0, atol=1e-8 * scale)

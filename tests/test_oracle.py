@@ -155,3 +155,15 @@ def test_plan_functions_match_reference(golden):
     for tag in ("smooth", "subset"):
         pb = O.pull_back(x0, x1, r.f, r.g, 0.05, r.center, r.cost_scale, p[f"log_v1_{tag}"])
         np.testing.assert_allclose(pb, p[f"pull_back_{tag}"], rtol=0, atol=1e-10)
+
+
+def test_local_pca_matches_reference(golden):
+    """The PCA restatement (randomized, transposed randomized, full and covariance-eigh solvers) against the
+    reference's local_pca_coords run on the same seeded expression."""
+    z = golden("pca_cases.npz")
+    for tag, (c0, c1, genes, seed) in synthetic.PCA_CASES.items():
+        e0, e1 = synthetic.expression(c0, c1, genes, seed)
+        p0, p1 = O.local_pca_coords(e0, e1, 30)
+        scale = np.abs(z[f"{tag}_p0"]).max()
+        np.testing.assert_allclose(p0, z[f"{tag}_p0"], rtol=0, atol=1e-8 * scale, err_msg=tag)
+        np.testing.assert_allclose(p1, z[f"{tag}_p1"], rtol=0, atol=1e-8 * scale, err_msg=tag)

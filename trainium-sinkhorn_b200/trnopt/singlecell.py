@@ -12,8 +12,91 @@ import time
 from dataclasses import dataclass, replace
 
 import numpy as np
+import torch
 
 from .sinkhorn import SinkhornOptions, SinkhornResult, normalization, sinkhorn, transport_plan
+
+
+PCA_RANDOM_STATE = 58951      # singlecell.py:42 (wot.ot.compute_pca's seed)
+
+
+def local_pca_coords(X0, X1, n_components: int = 30) -> tuple[np.ndarray, np.ndarray]:
+    """wot's per-pair embedding (singlecell.py:30-43): PCA of the two time points' expression together, fitted on
+    the transpose (genes as samples, cells as features) after centring each gene, as wot.ot.compute_pca does with
+    sklearn's PCA(n_components, random_state=58951); the cells' coordinates are the components scaled by the
+    singular values. Returns (cells0 x k, cells1 x k) in float64.
+
+    The arithmetic runs on the current CUDA device in float64 and follows the solver sklearn's PCA picks for the
+    shape (its `auto` policy): `randomized` for the usual sizes (the same Gaussian test matrix, drawn on the host
+    from RandomState(58951), LU-normalised power iterations, economic QR, thin SVD, sign flip on the rows of Vt),
+    `full` for small problems, `covariance_eigh` for few cells and many genes."""
+    import scipy.sparse as sp
+    if not torch.cuda.is_available():
+        raise RuntimeError("local_pca_coords needs a CUDA device (no CPU path in this package)")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    m1 = X0.toarray() if sp.issparse(X0) else np.asarray(X0)
+    m2 = X1.toarray() if sp.issparse(X1) else np.asarray(X1)
+    n0 = len(m1)
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a, dtype=np.float64)).to(dev)
+    x = torch.cat([t(m1), t(m2)])                      # cells x genes
+    x = x - x.mean(dim=0)
+    k = min(n_components, x.shape[0])
+    A = x.T                                            # sklearn's X: genes (samples) x cells (features)
+    n_samples, n_features = A.shape
+    if n_features <= 1000 and n_samples >= 10 * n_features:
+        solver = "covariance_eigh"
+    elif max(A.shape) <= 500:
+        solver = "full"
+    elif 1 <= k < 0.8 * min(A.shape):
+        solver = "randomized"
+    else:
+        solver = "full"
+    mean = A.mean(dim=0)
+    if solver == "full":
+        _, S, Vt = torch.linalg.svd(A - mean, full_matrices=False)
+    elif solver == "covariance_eigh":
+        C = A.T @ A - n_samples * torch.outer(mean, mean)
+        C = C / (n_samples - 1)
+        ev, vecs = torch.linalg.eigh(C)
+        ev, vecs = torch.flip(ev, dims=[0]), torch.flip(vecs, dims=[1])
+        ev = torch.clamp(ev, min=0.0)
+        S, Vt = torch.sqrt(ev * (n_samples - 1)), vecs.T
+    else:
+        S, Vt = _randomized_svd(A - mean, k, np.random.RandomState(PCA_RANDOM_STATE), dev)
+    Vt = _flip_rows(Vt)
+    comp = (Vt[:k].T * S[:k][None, :]).cpu().numpy()
+    return comp[:n0], comp[n0:]
+
+
+def _randomized_svd(M: torch.Tensor, k: int, rs: np.random.RandomState, dev, n_oversamples: int = 10):
+    """Halko et al.'s randomized SVD as sklearn.utils.extmath._randomized_svd runs it for PCA (n_iter 'auto',
+    LU normaliser, transpose 'auto', no sign flip inside): returns (s[:k], Vt[:k]) of M."""
+    n_random = k + n_oversamples
+    n_iter = 7 if k < 0.1 * min(M.shape) else 4
+    transpose = M.shape[0] < M.shape[1]
+    if transpose:
+        M = M.T
+    Q = torch.as_tensor(rs.normal(size=(M.shape[1], n_random))).to(dev)
+    def lu_pl(a):
+        P, L, _ = torch.linalg.lu(a)
+        return P @ L
+    norm = lu_pl if n_iter > 2 else (lambda a: a)
+    for _ in range(n_iter):
+        Q = norm(M @ Q)
+        Q = norm(M.T @ Q)
+    Q, _ = torch.linalg.qr(M @ Q, mode="reduced")
+    Uhat, s, Vt = torch.linalg.svd(Q.T @ M, full_matrices=False)
+    U = Q @ Uhat
+    if transpose:
+        return s[:k], U[:, :k].T
+    return s[:k], Vt[:k]
+
+
+def _flip_rows(Vt: torch.Tensor) -> torch.Tensor:
+    """sklearn's svd_flip(u_based_decision=False): each row's largest-|.| entry made positive."""
+    idx = torch.argmax(Vt.abs(), dim=1)
+    signs = torch.sign(Vt[torch.arange(Vt.shape[0], device=Vt.device), idx])
+    return Vt * signs[:, None]
 
 
 def wot_eps_stages(eps: float, eps0: float = 1.0, scalings: int = 5) -> tuple:

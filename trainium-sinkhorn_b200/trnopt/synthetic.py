@@ -91,3 +91,25 @@ def cfg5_eps_stages(eps_start: float = 1.0, eps_end: float = 0.01, stages: int =
     the last) go to SinkhornOptions.eps_stages, the last is SinkhornOptions.eps."""
     e = np.geomspace(eps_start, eps_end, stages)
     return tuple(float(v) for v in e[:-1])
+
+
+# Test shapes for local_pca_coords, one per solver sklearn's PCA picks: (cells0, cells1, genes, seed).
+PCA_CASES = {"randomized": (300, 400, 1200, 11), "randomized_t": (500, 400, 600, 12), "full": (80, 100, 300, 13),
+             "covariance_eigh": (50, 70, 2400, 14)}
+
+
+def expression(cells0: int, cells1: int, genes: int, seed: int = 0, factors: int = 12):
+    """Seeded synthetic expression for two time points (cells x genes, float64): log1p of Poisson counts whose rates
+    come from a low-rank model (cell-state factors drifting between the time points times gene loadings), the shape
+    of the wot inputs to local_pca_coords (a stand-in for the reprogramming data, which is absent)."""
+    rng = np.random.default_rng(seed)
+    load = rng.gamma(0.6, 1.0, size=(factors, genes))
+    base = rng.normal(-1.0, 0.6, size=genes)
+
+    def cells(n, shift):
+        z = rng.normal(0.0, 1.0, size=(n, factors)) * 0.5 + shift
+        rate = np.exp(np.clip(base[None, :] + 0.4 * z @ load / np.sqrt(factors), -8, 6))
+        return np.log1p(rng.poisson(rate)).astype(np.float64)
+
+    drift = rng.normal(0.0, 0.3, size=factors)
+    return cells(cells0, 0.0), cells(cells1, drift)
