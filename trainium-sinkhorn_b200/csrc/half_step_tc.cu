@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t lane_base = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(wg * (TC_BN / 2));
     const float dot2 = p.dot2;
     int T = 0;
-    bool ok = true;
+    bool ok = true, published = false;
     for (long long u = u_begin; u < u_end;) {
       const int r = (int)(u / sk.nct);
       const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
@@ -652,12 +652,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int row = r * TC_BM + qrow;
         if (row < p.rows) {
           const float v = finish_row(p, row, base + qrow, expected, TC_BM);
-          if (args.pub.world > 1) publish_row(args.pub, row, v);
+          if (args.pub.world > 1) {
+            publish_row(args.pub, row, v);
+            published = true;
+          }
         }
         if (qrow == 0) sk.counters[r] = 0;
       }
     }
-    if (args.pub.world > 1) __threadfence_system();   // this thread's peer stores, before the CTA barrier below
+    if (published) __threadfence_system();   // this thread's peer stores, before the CTA barrier below
   }
 
   tmem_fence_before();
