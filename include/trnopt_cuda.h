@@ -50,7 +50,8 @@ const char* trnopt_status_string(int status);
 int trnopt_last_cuda_error(void);
 
 /* Synchronises `stream`, then reads and clears the device error word of the current device: bit 1 = a bounded
- * wait inside a kernel gave up, bit 2 = tensor-memory allocation gave up, bit 4 = a launch invariant failed.
+ * wait inside a kernel gave up, bit 2 = tensor-memory allocation gave up, bit 4 = a launch invariant failed,
+ * bit 8 = another GPU of a sharded run did not publish its rows in time.
  * The reference has no device-side errors; its failures are Python exceptions (sinkhorn.py:201-207). */
 int trnopt_device_error_flags(void* stream, int* flags_out);
 
@@ -87,7 +88,8 @@ int trnopt_pack_cloud(const float* xT, int ldx, int n, int d, int scale_exp, voi
 
 /* The fused half-step on tcgen05 tensor cores (same contract as trnopt_half_step, sinkhorn.py:108-119 /
  * nki_sinkhorn.py:175-228): x . y as xh.yh + xh.yl + xl.yh in FP16 with FP32 accumulation (about 22 significant
- * bits), bias gh / eps + log b added in FP32, online row log-sum-exp. xpack = rows packed rows of this side
+ * bits), the bias gh / eps + log b added in the accumulator by one more MMA of its three-part BF16 split (24
+ * significant bits), online row log-sum-exp. xpack = rows packed rows of this side
  * (scale sx), ypack = m packed rows of the other side (scale sy). Needs an sm_100 device; workspace from
  * trnopt_workspace_size(rows, m, d, TRNOPT_PATH_TC). */
 int trnopt_half_step_tc(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
