@@ -11,14 +11,16 @@
 // Per CTA (one per SM, persistent over a stream-K range of (128-row tile, 256-column tile) units):
 //   warp 8      TMA producer: row tiles (A, two buffers) and column tiles (B, a ring of stages) into 128B-swizzled
 //               shared memory.
-//   warp 10     the tile's column bias (gh / eps + log b) * log2(e) into a 4-slot shared-memory ring.
-//   warp 9      allocates 512 TMEM columns and issues the MMAs (M 128, N 256, K 16; 3 dk / 16 per tile) into one
-//               of two 128 x 256 FP32 accumulators, committing to mbarriers.
+//   warp 10     the tile's column bias b_j = (gh_j / eps + log b_j) log2(e), written as b_j / dot2 in three BF16
+//               parts into one of two MMA operand slots (K 0..2 of row j).
+//   warp 9      allocates 512 TMEM columns and issues the MMAs (M 128, N 256, K 16; 3 dk / 16 FP16 MMAs per tile,
+//               then one BF16 MMA of a constant [1, 1, 1, 0 ...] tile with the bias slot, which adds b_j / dot2)
+//               into one of two 128 x 256 FP32 accumulators, committing to mbarriers.
 //   warps 0-7   two epilogue warpgroups, each on half the columns of every tile: a thread owns one row, reads its
-//               128 scores of a tile from TMEM 64 at a time, adds the bias in FP32 and folds them into an online
+//               128 scores of a tile from TMEM 64 at a time, scales them by dot2 and folds them into an online
 //               (max, sum) in base 2 (MUFU ex2, lazy max; see lse_tile128). The accumulator is released as soon
-//               as the tile's TMEM reads are done, before the last exps. At the end of a segment each warpgroup writes its partial; the last arrival for
-//               a row tile merges all partials and writes fh (common.cuh).
+//               as the tile's TMEM reads are done, before the last exps. At the end of a segment each warpgroup
+//               writes its partial; the last arrival for a row tile merges all partials and writes fh (common.cuh).
 // Every mbarrier wait is bounded (common.cuh kWaitLimitNs); a timeout sets the device error word and the CTA
 // unwinds (waits for its own copies and MMAs, frees TMEM) instead of hanging.
 #include <cuda.h>
