@@ -41,7 +41,8 @@ __global__ void comm_arrive_kernel(Publish pub) {
     if (q != pub.rank) st_release_sys(pub.flag_peer[q], pub.epoch);
 }
 
-// Hold the stream until every other rank's slot reaches pub.wait_epoch (bounded; kErrPeerTimeout on expiry).
+// Hold the stream until every other rank's slot reaches pub.wait_epoch (one warp; bounded, kErrPeerTimeout on
+// expiry).
 __global__ void comm_wait_kernel(Publish pub, int* error_word) { wait_peers(pub, error_word); }
 
 Publish make_publish(const Comm& c, const float* out) {
@@ -152,7 +153,7 @@ int trnopt_comm_wait(void* comm, void* stream) {
   if (c->world == 1) return TRNOPT_OK;
   Publish p = make_publish(*c, nullptr);
   p.wait_epoch = c->epoch;
-  comm_wait_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p, device_error_word());
+  comm_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p, device_error_word());
   return status_of(cudaGetLastError());
 }
 

@@ -171,20 +171,25 @@ __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned l
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Wait (one thread) until every other GPU's slot reaches pub.wait_epoch. Bounded: false after kWaitLimitNs, with
-// kErrPeerTimeout set in the error word.
+// Wait (all 32 lanes of a warp) until every other GPU's slot reaches pub.wait_epoch: lane q watches GPU q, so the
+// wait lasts as long as the latest GPU, not the sum of the polls. Bounded: false on every lane after kWaitLimitNs,
+// with kErrPeerTimeout set in the error word. Loads after it, by any lane, see the peers' rows (__syncwarp).
 __device__ inline bool wait_peers(const Publish& pub, int* error_word) {
+  const int lane = threadIdx.x & 31;
+  const bool watch = lane < pub.world && lane != pub.rank;
   const unsigned long long t0 = globaltimer_ns();
-  for (int q = 0; q < pub.world; ++q) {
-    if (q == pub.rank) continue;
-    while (ld_acquire_sys(pub.flags + q) < pub.wait_epoch) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        atomicOr(error_word, (int)kErrPeerTimeout);
-        return false;
-      }
-      __nanosleep(64);
+  bool mine = !watch;
+  for (;;) {
+    if (!mine) mine = ld_acquire_sys(pub.flags + lane) >= pub.wait_epoch;
+    if (__all_sync(0xffffffffu, mine)) break;
+    if (__any_sync(0xffffffffu, globaltimer_ns() - t0 > kWaitLimitNs)) {   // one decision for the whole warp
+      if (lane == 0) atomicOr(error_word, (int)kErrPeerTimeout);
+      __syncwarp();
+      return false;
     }
+    __nanosleep(64);
   }
+  __syncwarp();
   return true;
 }
 
@@ -195,10 +200,11 @@ __device__ __forceinline__ void publish_row(const Publish& pub, int row, float v
 }
 
 // Called by one thread of each CTA after the CTA's last publish_row (every writer has executed
-// __threadfence_system() and passed a CTA barrier since). The last CTA of the grid raises this GPU's slot to
-// pub.epoch on every other GPU and re-arms the counter.
+// __threadfence_system(), so its peer stores are complete, and passed a CTA barrier since; a GPU-scope fence
+// orders this CTA's arrival after them). The last CTA of the grid raises this GPU's slot to pub.epoch on every
+// other GPU (system-scope release) and re-arms the counter.
 __device__ inline void publish_done(const Publish& pub) {
-  __threadfence_system();
+  __threadfence();
   if (atomicAdd(pub.done, 1) == (int)gridDim.x - 1) {
     __threadfence_system();
     for (int q = 0; q < pub.world; ++q)

@@ -524,10 +524,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (args.pub.world > 1) {
       // gh is complete once every other GPU has published its rows of it (their stores land in this GPU's copy;
       // the loads below go through L2, never a stale L1 line)
-      int w = 1;
-      if (lane == 0) w = wait_peers(args.pub, p.error_word) ? 1 : 0;
-      w = __shfl_sync(0xffffffffu, w, 0);
-      if (!w) {
+      if (!wait_peers(args.pub, p.error_word)) {
         *abort_flag = 1;
         ok = false;
       }

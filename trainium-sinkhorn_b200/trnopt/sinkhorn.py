@@ -16,9 +16,11 @@ frame); this keeps |x|^2 and x.y small and is what the reference's own normaliza
 (sinkhorn.py:224-225). The returned f, g, center and cost_scale are the reference's.
 
 Multi-GPU. With opts.cores = P > 1 the call must be made on every rank of an initialised torch.distributed
-process group of P ranks (one GPU each, same inputs): each rank computes 1/P of the rows of every half-step and the
-new potential is all-gathered over NCCL, as the reference splits rows across NeuronCores and exchanges the halves
-(sinkhorn.py:295-311).
+process group of P ranks (one GPU each, same inputs): each rank computes 1/P of the rows of every half-step, as the
+reference splits rows across NeuronCores and exchanges the halves (sinkhorn.py:295-311). The new potential reaches
+every GPU either from the half-step kernel itself, which stores its rows into every GPU's copy over NVLink and
+raises an epoch flag that the next half-step waits for (opts.cuda_exchange "peer", the default on the tensor-core
+path), or by an NCCL all-gather after each half-step ("nccl").
 """
 
 from __future__ import annotations
