@@ -224,8 +224,9 @@ __device__ __forceinline__ float exp_sum(const float (&a)[N], float off) {
 // Redo of one 64-value block in absolute terms from the raw accumulators re-read from TMEM; returns the new
 // (M, L). The relative values lose their low bits when M is far below the block (e.g. M set by columns of
 // PAD_LOG_WEIGHT, -1e9). Warp-uniform entry (tcgen05.ld is .sync.aligned); lanes without `redo` get (M, L) back
-// unchanged.
-__device__ __forceinline__ float2 block_redo(uint32_t taddr, float dot2, bool redo, float M, float L) {
+// unchanged. Rarely taken, so it is a call rather than inlined: its two copies would otherwise sit in the hot loop's
+// code (inlined, the kernel measured ~3 % slower).
+static __device__ __noinline__ float2 block_redo(uint32_t taddr, float dot2, bool redo, float M, float L) {
   constexpr int N = 64;
   uint32_t raw[N];
   TRNOPT_TMEM_LD64(taddr, raw);
