@@ -11,9 +11,10 @@ Workloads (synthetic, seeded; trnopt.synthetic):
         iterations, tol 1e-8): a step is the whole map through the public API, reported in seconds
   cfg4  the 38-pair trajectory pipeline (175k cells) with cfg3's settings: a step is the whole pipeline, seconds
 A step is one Sinkhorn iteration with the inputs resident in HBM; L2 (126 MB) is flushed between timed steps by
-writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU, rows of every
-half-step are split across the ranks and the new potential is all-gathered with NCCL; the reported time is the
-max over ranks.
+writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU and rows of every
+half-step are split across the ranks; each GPU's new rows reach the others through peer stores from the half-step
+kernel (--exchange peer, the default on the tensor-core path) or one NCCL all-gather per half-step (--exchange
+nccl); the reported time is the max over ranks.
 
 --impl reference times the reference's CPU solver on this host's cores (the CPU port in oracle/, float32, all
 threads) on the same workload; under torchrun only rank 0 runs it.
@@ -426,14 +427,21 @@ def run_ours(args, rank, world, dev):
     if not args.no_e2e:
         opts = SinkhornOptions(max_iters=args.steps, fixed_iters=True, backend=Backend.preset("cuda-fused", device=str(dev)),
                                cores=world, cuda_path=path, cuda_exchange=args.exchange, **kw)
+        # the clouds in pinned (page-locked) host memory, as a caller feeding a GPU solver keeps them: the upload
+        # inside sinkhorn() is then one DMA per cloud
+        def pinned(a):
+            t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
+            t.numpy()[...] = a
+            return t.numpy()
+        xh, yh = pinned(x), pinned(y)
         for _ in range(max(1, min(args.warmup, 3))):      # warm-up solves of the same problem, untimed
-            sinkhorn(x, y, opts=SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend, cores=world,
-                                                cuda_path=path, cuda_exchange=args.exchange, **kw))
+            sinkhorn(xh, yh, opts=SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend, cores=world,
+                                                  cuda_path=path, cuda_exchange=args.exchange, **kw))
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        r = sinkhorn(x, y, opts=opts)
+        r = sinkhorn(xh, yh, opts=opts)
         torch.cuda.synchronize(dev)
         dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
         if world > 1:
@@ -442,7 +450,7 @@ def run_ours(args, rank, world, dev):
         d2h = 8 * (n + m)                                 # f and g in float64
         e2e = {"value": float(dt.item()) * 1e3 / r.iterations, "unit": "ms/iter",
                "h2d_bytes_per_step": h2d / r.iterations, "d2h_bytes_per_step": d2h / r.iterations,
-               "note": "one public sinkhorn() call on host float64 arrays after untimed 2-iteration warm-up calls of "
+               "note": "one public sinkhorn() call on host float64 arrays (pinned memory) after untimed 2-iteration warm-up calls of "
                        "the same problem (upload, normalisation, padding, "
                        f"{r.iterations} fixed iterations, f and g back to the host), divided by the iterations"}
 
