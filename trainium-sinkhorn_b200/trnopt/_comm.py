@@ -77,13 +77,20 @@ _REGIONS: dict = {}
 
 
 def region(nbytes: int, group=None) -> PeerRegion:
-    """The process's region for `group` on the current device, created or grown (collectively) to nbytes."""
-    key = (id(group), torch.cuda.current_device())
+    """The process's region for `group` on the current device, created or grown (collectively) to nbytes. The
+    default group is resolved to the process group object itself, so a re-initialised default group (with possibly
+    another world size) gets its own region rather than one mapped for the previous group's ranks."""
+    import torch.distributed as dist
+    g = group if group is not None else dist.group.WORLD
+    key = (id(g), torch.cuda.current_device())
     r = _REGIONS.get(key)
+    if r is not None and r.group_obj is not g:      # the id of a dead group reused by a new object
+        r = None
     if r is not None and r.nbytes >= nbytes:
         return r
     if r is not None:
         r.close()
         nbytes = max(nbytes, 2 * r.nbytes)
     r = _REGIONS[key] = PeerRegion(nbytes, group)
+    r.group_obj = g
     return r
