@@ -3,13 +3,17 @@
 The same functions and formulation as the reference's src/trnopt/singlecell.py (wot, Schiebinger et al. 2019):
 cost = squared distance / its exact median (computed once per pair, on the GPU), uniform reference measure,
 row target = growth G / I, column target = mean(G) / J, KL penalties (lambda1, lambda2), wot's eps stages, and
-growth iterations that set the next row target to the previous plan's row sums.
+growth iterations that set the next row target to the previous plan's row sums. `wot_trajectory` runs the maps of
+every consecutive pair of a time course (the loop of the reference's examples/singlecell_wot.py) and can write each
+pair's potentials in that example's npz layout and restart from them (`save_pair`, `load_pair`).
 """
 
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, replace
+from pathlib import Path
 
 import numpy as np
 import torch
@@ -143,3 +147,111 @@ def wot_tmap(x0, x1, tm: TransportMap) -> np.ndarray:
     """The dense transport map in wot's normalization (I * P), on the host; small pairs only (singlecell.py:89-92)."""
     I, J = len(x0), len(x1)
     return I * transport_plan(x0, x1, tm.result, np.full(I, 1.0 / I), np.full(J, 1.0 / J))
+
+
+# The keys of the reference example's per-pair files (examples/singlecell_wot.py:112-117).
+PAIR_KEYS = ("f", "g", "eps", "center", "cost_scale", "row_mass", "col_mass", "learned_growth", "cells0", "cells1",
+             "x0", "x1")
+
+
+@dataclass
+class SavedPair:
+    tm: TransportMap
+    x0: np.ndarray
+    x1: np.ndarray
+    cells0: np.ndarray
+    cells1: np.ndarray
+
+
+def pair_path(directory, t0: float, t1: float) -> Path:
+    """directory / pair_{t0:g}_{t1:g}.npz, the reference example's file name (examples/singlecell_wot.py:114)."""
+    return Path(directory) / f"pair_{t0:g}_{t1:g}.npz"
+
+
+def save_pair(path, tm: TransportMap, x0, x1, cells0=None, cells1=None) -> Path:
+    """Write one pair's potentials, masses and learned growth under the reference example's keys (PAIR_KEYS), plus
+    `iterations`, `seconds`, `rho`, `error` and `converged`. Cell names are stored as unicode arrays (no pickled
+    objects; None stores the row indices). The file appears whole or not at all (written beside it, then renamed),
+    so a pipeline killed mid-write leaves nothing that a restart would half-read."""
+    r = tm.result
+    x0, x1 = np.asarray(x0, dtype=np.float64), np.asarray(x1, dtype=np.float64)
+    c0 = np.arange(len(x0)).astype(str) if cells0 is None else np.asarray(cells0, dtype=str)
+    c1 = np.arange(len(x1)).astype(str) if cells1 is None else np.asarray(cells1, dtype=str)
+    none = np.zeros(0)
+    arrays = dict(f=r.f, g=r.g, eps=r.eps, center=r.center, cost_scale=r.cost_scale,
+                  row_mass=none if r.row_mass is None else r.row_mass,
+                  col_mass=none if r.col_mass is None else r.col_mass,
+                  learned_growth=np.array(tm.learned_growth), cells0=c0, cells1=c1, x0=x0, x1=x1,
+                  iterations=tm.iterations, seconds=tm.seconds,
+                  rho=np.array(np.nan if r.rho is None else r.rho, dtype=np.float64), error=r.error,
+                  converged=r.converged)
+    path = Path(path)
+    tmp = path.with_name(path.name + ".partial")
+    with open(tmp, "wb") as fh:
+        np.savez(fh, **arrays)
+    os.replace(tmp, path)
+    return path
+
+
+def load_pair(path, allow_pickle: bool = False) -> SavedPair:
+    """Read a file of save_pair or of the reference example. The reference stores cell names as object arrays, which
+    NumPy loads only with allow_pickle=True (pickles run code: pass it only for files you trust). Keys the reference
+    does not write come back as: iterations 0, seconds 0, rho None, error NaN, converged False."""
+    with np.load(path, allow_pickle=allow_pickle) as z:
+        missing = [k for k in PAIR_KEYS if k not in z.files]
+        if missing:
+            raise ValueError(f"{path}: not a pair file (missing {', '.join(missing)})")
+        d = {k: z[k] for k in z.files}
+    rho = None
+    if "rho" in d and not np.all(np.isnan(d["rho"])):
+        rho = tuple(float(v) for v in np.atleast_1d(d["rho"]))
+        rho = rho[0] if len(rho) == 1 else rho
+    mass = lambda v: None if v.size == 0 else v                  # noqa: E731
+    res = SinkhornResult(f=d["f"], g=d["g"], iterations=int(d.get("iterations", 0)), error=float(d.get("error", np.nan)),
+                         converged=bool(d.get("converged", False)), cost=float("nan"),
+                         seconds=float(d.get("seconds", 0.0)), eps=float(d["eps"]), rho=rho, center=d["center"],
+                         cost_scale=float(d["cost_scale"]), row_mass=mass(d["row_mass"]), col_mass=mass(d["col_mass"]))
+    tm = TransportMap(result=res, learned_growth=list(np.atleast_2d(d["learned_growth"])),
+                      seconds=float(d.get("seconds", 0.0)), iterations=int(d.get("iterations", 0)))
+    return SavedPair(tm=tm, x0=d["x0"], x1=d["x1"], cells0=d["cells0"], cells1=d["cells1"])
+
+
+def wot_trajectory(cohorts, times=None, growth=None, *, n_components: int | None = None, save=None,
+                   resume: bool = False, cells=None, **map_kwargs) -> list:
+    """Transport maps for every consecutive pair of a time course: the loop of the reference's
+    examples/singlecell_wot.py:79-117. cohorts[k] is the (cells, features) matrix at times[k] (default 0, 1, ...).
+    Per pair (t0, t1): with n_components, both cohorts are embedded by local_pca_coords (as the example does with
+    expression), else their rows are the coordinates; the growth rates growth[k] are raised to t1 - t0; one
+    wot_transport_map (map_kwargs: eps, lambda1, lambda2, growth_iters, tol, stage_tol, opts). With save=DIR each
+    pair is written to pair_path(DIR, t0, t1) (save_pair, cell names from cells[k] if given); with resume=True a pair
+    whose file exists is loaded instead of solved, so an interrupted run restarts at its first missing pair. A file
+    written for other coordinates raises ValueError. Returns the TransportMaps in pair order."""
+    times = list(range(len(cohorts))) if times is None else [float(t) for t in times]
+    if len(times) != len(cohorts):
+        raise ValueError(f"{len(cohorts)} cohorts but {len(times)} times")
+    if growth is not None and len(growth) < len(cohorts) - 1:
+        raise ValueError("growth needs one vector per cohort (the last is not used)")
+    if resume and save is None:
+        raise ValueError("resume=True needs save=DIR")
+    if save is not None:
+        Path(save).mkdir(parents=True, exist_ok=True)
+    maps = []
+    for k in range(len(cohorts) - 1):
+        t0, t1 = times[k], times[k + 1]
+        if n_components:
+            x0, x1 = local_pca_coords(cohorts[k], cohorts[k + 1], n_components)
+        else:
+            x0, x1 = np.asarray(cohorts[k], dtype=np.float64), np.asarray(cohorts[k + 1], dtype=np.float64)
+        path = None if save is None else pair_path(save, t0, t1)
+        if resume and path.exists():
+            sp = load_pair(path)
+            if sp.x0.shape != x0.shape or sp.x1.shape != x1.shape or not (
+                    np.array_equal(sp.x0, x0) and np.array_equal(sp.x1, x1)):
+                raise ValueError(f"{path} was written for other coordinates: remove it or pass resume=False")
+            maps.append(sp.tm)
+            continue
+        tm = wot_transport_map(x0, x1, None if growth is None else growth[k], t1 - t0, **map_kwargs)
+        if path is not None:
+            save_pair(path, tm, x0, x1, None if cells is None else cells[k], None if cells is None else cells[k + 1])
+        maps.append(tm)
+    return maps
