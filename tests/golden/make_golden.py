@@ -11,7 +11,8 @@ Files:
                         padded columns, off != 0 and kappa < 1, d in {5, 16, 30, 64}
   row_lse_kat.npz       the row-LSE known-answer inputs of examples/nki_sinkhorn_check.py:22-35 and the float64
                         answer (scipy logsumexp of xa^T ya)
-  solver_cases.npz      reference sinkhorn() on the cases of tests/test_sinkhorn.py (fp64 and fp32)
+  solver_cases.npz      reference sinkhorn() on the cases of tests/test_sinkhorn.py (fp64 and fp32, the eps-scaling
+                        case in both)
   cfg1.npz              config 1 (2,000^2, d 16, 200 fixed iterations, eps 0.1, raw cost): f, g in fp64 and fp32,
                         and the fp64 plan's row / column sums
   normalization.npz     normalization() scales (mean and median, odd and even n m, config 3's full pair)
@@ -141,6 +142,10 @@ def solver_cases():
     o = dict(eps=0.01, tol=1e-6, max_iters=20_000)
     _res("epsplain_f64", ref_sk.sinkhorn(x3, y3, opts=SO(**o)), out)
     _res("epsscaled_f64", ref_sk.sinkhorn(x3, y3, opts=SO(eps_start=2.0, eps_decay=0.8, **o)), out)
+    # the reference's own float32 runs of the eps case: at eps 0.01 float32 rounding alone moves the potentials by
+    # more than 1e-4 eps, so a float32 solver is held to this run's distance from the float64 one
+    _res("epsplain_f32", ref_sk.sinkhorn(x3, y3, opts=SO(backend=CPU32, **o)), out)
+    _res("epsscaled_f32", ref_sk.sinkhorn(x3, y3, opts=SO(eps_start=2.0, eps_decay=0.8, backend=CPU32, **o)), out)
     np.savez_compressed(HERE / "solver_cases.npz", **out)
 
 
