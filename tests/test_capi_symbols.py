@@ -1,4 +1,5 @@
-"""The C-ABI library loads without a GPU and exports every function include/trnopt_cuda.h declares. CPU only: no
+"""The C-ABI library loads without a GPU and exports every function include/trnopt_cuda.h declares, and the header
+compiles as C99 and C++11. CPU only: no
 compute call is made here."""
 
 import ctypes
@@ -36,3 +37,23 @@ def test_status_strings_without_gpu():
     assert _capi.lib.trnopt_status_string(0) == b"ok"
     assert _capi.lib.trnopt_status_string(-3) == b"workspace missing or too small"
     assert _capi.lib.trnopt_version() >= 100
+
+
+def test_header_compiles_as_c_and_cpp(tmp_path):
+    """The header is usable from plain C (cgo, JNI glue, plugin hosts written in C) and from C++: every declared
+    function is referenced through a function pointer, so a declaration that is not valid C fails here."""
+    import shutil
+    import subprocess
+    import pytest
+    names = declared_functions()
+    body = "typedef void (*fn)(void);\nconst fn every[] = {\n" + "".join(f"  (fn){n},\n" for n in names) + "};\n"
+    src = '#include "trnopt_cuda.h"\n' + body + "int main(void) { return (int)(sizeof every / sizeof every[0]) > 0 ? 0 : 1; }\n"
+    inc = str(ROOT / "include")
+    for compiler, ext, std in (("gcc", "c", "-std=c99"), ("g++", "cpp", "-std=c++11")):
+        if shutil.which(compiler) is None:
+            pytest.skip(f"{compiler} not installed")
+        f = tmp_path / f"use.{ext}"
+        f.write_text(src)
+        r = subprocess.run([compiler, std, "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", inc, "-c", str(f), "-o",
+                            str(tmp_path / f"use_{ext}.o")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
