@@ -1,6 +1,5 @@
 """The C-ABI library loads without a GPU and exports every function include/trnopt_cuda.h declares, and the header
-compiles as C99 and C++11. CPU only: no
-compute call is made here."""
+compiles as C99 and C++11. CPU only: no compute call is made here."""
 
 import ctypes
 import re
