@@ -421,6 +421,17 @@ def run_ours(args, rank, world, dev):
     if path == "ffma":
         roof["ffma"] = {"achieved_tflops": round(tflops, 2), "peak_tflops": round(ffma_peak, 2),
                         "frac": round(tflops / ffma_peak, 4)}
+    # The north star's roofline: the slowest of the contraction at its pipe's peak (useful FLOPs), the exps at the
+    # MUFU rate and the algorithmic bytes at the measured HBM copy rate (both clouds once, 4 bytes per coordinate
+    # in FP32 or as an FP16 hi/lo pair, plus the vectors: (n + m)(4d + 12) per launch); frac = that
+    # bound's time over the measured launch time.
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    bounds_us = {"contraction": flops / ((ffma_peak if path == "ffma" else bf16) * 1e12) * 1e6,
+                 "exp": exps / sfu_peak * 1e6,
+                 "hbm": (X.npad + Y.npad) * (4 * X.d + 12) / (hbm * 1e9) * 1e6}
+    slow = max(bounds_us, key=bounds_us.get)
+    roof["slowest_bound"] = {"name": slow, "bound_us": {k: round(v, 3) for k, v in bounds_us.items()},
+                             "launch_us": round(launch_ms * 1e3, 3), "frac": round(bounds_us[slow] / (launch_ms * 1e3), 4)}
 
     # End to end through the public API: host arrays in, potentials out, K iterations.
     e2e = None
