@@ -10,6 +10,8 @@ Workloads (synthetic, seeded; trnopt.synthetic):
   cfg3  one wot transport map, 7,355 x 8,962 cells in d = 30 (median cost, eps 0.05, lambda (1, 50), 3 growth
         iterations, tol 1e-8): a step is the whole map through the public API, reported in seconds
   cfg4  the 38-pair trajectory pipeline (175k cells) with cfg3's settings: a step is the whole pipeline, seconds
+  cfg2conv  config 2 to convergence: one sinkhorn() call from pinned host arrays, balanced marginal error below
+        tol 1e-6 checked every 10 iterations; a step is the whole solve, seconds (iterations in `config`)
 A step is one Sinkhorn iteration with the inputs resident in HBM; L2 (126 MB) is flushed between timed steps by
 writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU and rows of every
 half-step are split across the ranks; each GPU's new rows reach the others through peer stores from the half-step
@@ -49,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4", "cfg2conv"])
     ap.add_argument("--path", default="auto", choices=["auto", "ffma", "tc"])
     ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
                     help="N > 1: peer stores from the half-step kernels (tc path) or an NCCL all-gather per half-step")
@@ -267,11 +269,23 @@ def run_reference(args, rank, world):
 
 
 def run_pipeline(args, rank, world, dev):
-    """cfg3 / cfg4: wot transport maps through the public API (trnopt.singlecell), wall time per map / pipeline."""
-    from trnopt import Backend, SinkhornOptions, synthetic
+    """cfg3 / cfg4: wot transport maps through the public API (trnopt.singlecell), wall time per map / pipeline;
+    cfg2conv: one config-2 solve to convergence through sinkhorn()."""
+    from trnopt import Backend, SinkhornOptions, sinkhorn, synthetic
     from trnopt.singlecell import wot_trajectory, wot_transport_map
     opts = SinkhornOptions(backend=Backend.preset("cuda-fused", device=str(dev)), cores=world)
-    if args.workload == "cfg3":
+    last = {}
+    if args.workload == "cfg2conv":
+        def pinned(a):
+            t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
+            t.numpy()[...] = a
+            return t.numpy()
+        xc, yc = (pinned(a) for a in synthetic.cfg2())
+        conv = SinkhornOptions(eps=0.1, tol=1e-6, check_every=10, max_iters=20_000, normalize=False,
+                               backend=opts.backend, cores=world)
+        cfg = {"workload": "cfg2conv", "n": 10_000, "m": 10_000, "d": 64, "eps": 0.1, "tol": 1e-6, "check_every": 10,
+               "input": "host float64 arrays in pinned memory, f and g returned to the host"}
+    elif args.workload == "cfg3":
         x0, x1, g = synthetic.cfg3()
         pairs = [(x0, x1, g)]
         cfg = {"workload": "cfg3", "n": len(x0), "m": len(x1), "d": 30, "eps": 0.05, "lambda": [1.0, 50.0],
@@ -285,6 +299,10 @@ def run_pipeline(args, rank, world, dev):
     kw = dict(eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8, opts=opts)
 
     def one():
+        if args.workload == "cfg2conv":
+            r = sinkhorn(xc, yc, opts=conv)
+            last.update(converged=bool(r.converged), error=float(r.error))
+            return r.iterations
         if args.workload == "cfg4":          # the whole time course through the public pipeline loop
             return sum(tm.iterations for tm in wot_trajectory(tr.cohorts, None, tr.growth, **kw))
         return sum(wot_transport_map(x0, x1, g, **kw).iterations for x0, x1, g in pairs)
@@ -300,11 +318,13 @@ def run_pipeline(args, rank, world, dev):
         times.append(time.perf_counter() - t0)
     v = float(np.mean(times))
     if rank == 0:
-        line = {"metric": "wot transport map seconds" if args.workload == "cfg3" else "38-pair pipeline seconds",
+        metric = {"cfg3": "wot transport map seconds", "cfg4": "38-pair pipeline seconds",
+                  "cfg2conv": "config 2 time to convergence seconds"}[args.workload]
+        line = {"metric": metric,
                 "value": v, "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic (seeded generators in trnopt.synthetic)",
-                "config": {**cfg, "sinkhorn_iterations": iters, "ms_per_iteration": v * 1e3 / max(1, iters)},
+                "config": {**cfg, "sinkhorn_iterations": iters, "ms_per_iteration": v * 1e3 / max(1, iters), **last},
                 "gpu_launches": 2 * iters}
         print(json.dumps(line), flush=True)
 
@@ -498,7 +518,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     try:
-        if args.workload in ("cfg3", "cfg4"):
+        if args.workload in ("cfg3", "cfg4", "cfg2conv"):
             run_pipeline(args, rank, world, dev)
         else:
             run_ours(args, rank, world, dev)
