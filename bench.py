@@ -12,6 +12,9 @@ Workloads (synthetic, seeded; trnopt.synthetic):
   cfg4  the 38-pair trajectory pipeline (175k cells) with cfg3's settings: a step is the whole pipeline, seconds
   cfg2conv  config 2 to convergence: one sinkhorn() call from pinned host arrays, balanced marginal error below
         tol 1e-6 checked every 10 iterations; a step is the whole solve, seconds (iterations in `config`)
+  cfg5conv  config 5's schedule: eps 1.0 -> 0.01 over 8 geometric values, at most 50 iterations per intermediate
+        value (a stage also ends when its potential change falls below the float32 stage floor), 400 iterations
+        in all, mean-normalised cost; a step is the whole solve, seconds
 A step is one Sinkhorn iteration with the inputs resident in HBM; L2 (126 MB) is flushed between timed steps by
 writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU and rows of every
 half-step are split across the ranks; each GPU's new rows reach the others through peer stores from the half-step
@@ -51,7 +54,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4", "cfg2conv"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4", "cfg2conv", "cfg5conv"])
     ap.add_argument("--path", default="auto", choices=["auto", "ffma", "tc"])
     ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
                     help="N > 1: peer stores from the half-step kernels (tc path) or an NCCL all-gather per half-step")
@@ -275,15 +278,23 @@ def run_pipeline(args, rank, world, dev):
     from trnopt.singlecell import wot_trajectory, wot_transport_map
     opts = SinkhornOptions(backend=Backend.preset("cuda-fused", device=str(dev)), cores=world)
     last = {}
+    def pinned(a):
+        t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
+        t.numpy()[...] = a
+        return t.numpy()
     if args.workload == "cfg2conv":
-        def pinned(a):
-            t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
-            t.numpy()[...] = a
-            return t.numpy()
         xc, yc = (pinned(a) for a in synthetic.cfg2())
         conv = SinkhornOptions(eps=0.1, tol=1e-6, check_every=10, max_iters=20_000, normalize=False,
                                backend=opts.backend, cores=world)
         cfg = {"workload": "cfg2conv", "n": 10_000, "m": 10_000, "d": 64, "eps": 0.1, "tol": 1e-6, "check_every": 10,
+               "input": "host float64 arrays in pinned memory, f and g returned to the host"}
+    elif args.workload == "cfg5conv":
+        xc, yc = (pinned(a) for a in synthetic.cfg5())
+        stages = synthetic.cfg5_eps_stages()
+        conv = SinkhornOptions(eps=0.01, eps_stages=stages, stage_max_iters=50, max_iters=400, fixed_iters=True,
+                               normalize="mean", backend=opts.backend, cores=world)
+        cfg = {"workload": "cfg5conv", "n": len(xc), "m": len(yc), "d": 64, "eps": 0.01,
+               "eps_stages": [round(e, 6) for e in stages], "stage_max_iters": 50, "iterations_in_all": 400,
                "input": "host float64 arrays in pinned memory, f and g returned to the host"}
     elif args.workload == "cfg3":
         x0, x1, g = synthetic.cfg3()
@@ -299,7 +310,7 @@ def run_pipeline(args, rank, world, dev):
     kw = dict(eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8, opts=opts)
 
     def one():
-        if args.workload == "cfg2conv":
+        if args.workload in ("cfg2conv", "cfg5conv"):
             r = sinkhorn(xc, yc, opts=conv)
             last.update(converged=bool(r.converged), error=float(r.error))
             return r.iterations
@@ -319,7 +330,8 @@ def run_pipeline(args, rank, world, dev):
     v = float(np.mean(times))
     if rank == 0:
         metric = {"cfg3": "wot transport map seconds", "cfg4": "38-pair pipeline seconds",
-                  "cfg2conv": "config 2 time to convergence seconds"}[args.workload]
+                  "cfg2conv": "config 2 time to convergence seconds",
+                  "cfg5conv": "config 5 eps-staged solve seconds"}[args.workload]
         line = {"metric": metric,
                 "value": v, "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
@@ -518,7 +530,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     try:
-        if args.workload in ("cfg3", "cfg4", "cfg2conv"):
+        if args.workload in ("cfg3", "cfg4", "cfg2conv", "cfg5conv"):
             run_pipeline(args, rank, world, dev)
         else:
             run_ours(args, rank, world, dev)
