@@ -1,33 +1,35 @@
 """Benchmark: Sinkhorn ms per iteration (one f half-step + one g half-step) on the fused CUDA half-step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload auto|cfg2|cfg5|weak]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload auto|...]
 
-Workloads (synthetic, seeded; trnopt.synthetic):
-  cfg2  n = m = 10,000, d = 64, x, y ~ U[0,1]^64, eps 0.1, raw cost (the N = 1 default)
-  weak  the N > 1 default: n = 10,000 N rows, m = 10,000, d = 64 (config 2's per-GPU work at every N)
-  cfg5  n = m = 262,144, d = 64, x, y ~ N(0, I)/8, mean-normalised cost, eps 0.01 (strong
-        scaling over N)
-  cfg3  one wot transport map, 7,355 x 8,962 cells in d = 30 (median cost, eps 0.05, lambda (1, 50), 3 growth
-        iterations, tol 1e-8): a step is the whole map through the public API, reported in seconds
-  cfg4  the 38-pair trajectory pipeline (175k cells) with cfg3's settings: a step is the whole pipeline, seconds
-  cfg2conv  config 2 to convergence: one sinkhorn() call from pinned host arrays, balanced marginal error below
-        tol 1e-6 checked every 10 iterations; a step is the whole solve, seconds (iterations in `config`)
-  cfg5conv  config 5's schedule: eps 1.0 -> 0.01 over 8 geometric values, at most 50 iterations per intermediate
-        value (a stage also ends when its potential change falls below the float32 stage floor), 400 iterations
-        in all, mean-normalised cost; a step is the whole solve, seconds
-A step is one Sinkhorn iteration with the inputs resident in HBM; L2 (126 MB) is flushed between timed steps by
-writing a 256 MB buffer (outside the timed region). Under torchrun each rank drives one GPU and rows of every
-half-step are split across the ranks; each GPU's new rows reach the others through peer stores from the half-step
-kernel (--exchange peer, the default on the tensor-core path) or one NCCL all-gather per half-step (--exchange
-nccl); the reported time is the max over ranks.
+The metric has three clauses: ms/iter at 10k^2 d = 64 on one B200, ms/iter at 262k^2 d = 64 on
+1/2/4/8 B200s, and the 38-pair pipeline in seconds. `value` is the first clause on a plain run and the second under
+torchrun; the other clauses ride along in the same line.
 
---impl reference times the reference's CPU solver on this host's cores (the CPU port in oracle/, float32, all
-threads) on the same workload; under torchrun only rank 0 runs it.
+Workloads (synthetic, seeded; trainium-sinkhorn_b200/trnopt/synthetic.py):
+  cfg2  n = m = 10,000, d = 64, x, y ~ U[0,1]^64, eps 0.1, raw cost: the default of a plain
+        `python bench.py` (one GPU)
+  cfg5  n = m = 262,144, d = 64, x, y ~ N(0, I)/8, mean-normalised cost, eps 0.01: the default
+        under torchrun (N = 1, 2, 4, 8: strong scaling, the rows of every half-step split over the GPUs)
+  weak  n = 10,000 N rows, m = 10,000, d = 64 (config 2's work on every GPU)
+  cfg3, cfg4, cfg2conv, cfg5conv: one line each for a whole solve through the public API, in seconds (config 3's
+        wot transport map, the 38-pair pipeline, config 2 to tol 1e-6, config 5's eps-staged 400-iteration solve).
+        The default cfg2 line carries all four as sub-objects; the default cfg5 line carries cfg5conv.
+
+A step is one Sinkhorn iteration with the clouds resident in HBM; L2 (126 MB) is flushed between timed steps by
+writing a 256 MB buffer (outside the timed region); CUDA events on the launching stream time each step; the
+reported time is the max over ranks. Under torchrun each rank drives one GPU; each GPU's new rows reach the others
+through peer stores from the half-step kernel (--exchange peer, the default on the tensor-core path) or one NCCL
+all-gather per half-step (--exchange nccl).
+
+--impl reference times the reference's CPU solver (the CPU port in oracle/, float32, all host threads) on the same
+workload and config; it imports neither this package nor its library. Under torchrun only rank 0 runs it.
 """
 
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -39,13 +41,14 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, str(ROOT / "trainium-sinkhorn_b200"))
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "Sinkhorn ms/iter (10k^2 d=64; 262k^2 d=64 @1/2/4/8 B200)"
 SMS = 148
+MUFU_PER_CLK = 16                 # ex2 results per clock per SM
+L2_NOTE = "GPU arm: L2 flushed between timed steps (256 MB write); CPU arm: host memory"
 
 
 def parse():
@@ -54,30 +57,64 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4", "cfg2conv", "cfg5conv"])
+    ap.add_argument("--workload", default="auto",
+                    choices=["auto", "cfg2", "cfg5", "weak", "cfg3", "cfg4", "cfg2conv", "cfg5conv"])
     ap.add_argument("--path", default="auto", choices=["auto", "ffma", "tc"])
     ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
                     help="N > 1: peer stores from the half-step kernels (tc path) or an NCCL all-gather per half-step")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the convergence / pipeline / parity sub-objects")
     ap.add_argument("--no-flush", action="store_true", help="(profiling runs only) do not flush L2 between steps")
     return ap.parse_args()
 
 
-def workload(name: str, world: int):
-    from trnopt import synthetic
-    if name == "auto":
-        name = "cfg2" if world == 1 else "weak"
-    if name == "cfg2":
-        x, y = synthetic.cfg2()
-        return name, x, y, dict(eps=0.1, normalize=False), {"n": 10_000, "m": 10_000, "d": 64, "eps": 0.1}
-    if name == "weak":
-        x, y = synthetic.cfg2(n=10_000 * world, m=10_000)
-        return name, x, y, dict(eps=0.1, normalize=False), {"n": 10_000 * world, "m": 10_000, "d": 64, "eps": 0.1}
-    x, y = synthetic.cfg5()
-    return name, x, y, dict(eps=0.01, normalize="mean"), {"n": len(x), "m": len(y), "d": 64, "eps": 0.01}
+def synthetic():
+    """The seeded generators, loaded from their file: this module must not import the trnopt package (which loads the
+    CUDA library) in the reference arm."""
+    mod = sys.modules.get("_bench_synthetic")
+    if mod is None:
+        spec = importlib.util.spec_from_file_location(
+            "_bench_synthetic", ROOT / "trainium-sinkhorn_b200" / "trnopt" / "synthetic.py")
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["_bench_synthetic"] = mod
+        spec.loader.exec_module(mod)
+    return mod
 
+
+def under_torchrun() -> bool:
+    return "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+
+
+def resolve_workload(name: str, world: int) -> str:
+    if name == "auto":
+        return "cfg5" if (world > 1 or under_torchrun()) else "cfg2"
+    return name
+
+
+def workload(name: str, world: int):
+    """(x, y, solver kwargs, config) of an iteration workload. The config is the same in both arms."""
+    S = synthetic()
+    if name == "cfg2":
+        x, y = S.cfg2()
+        kw, cost = dict(eps=0.1, normalize=False), "squared euclidean (raw)"
+    elif name == "weak":
+        x, y = S.cfg2(n=10_000 * world, m=10_000)
+        kw, cost = dict(eps=0.1, normalize=False), "squared euclidean (raw)"
+    elif name == "cfg5":
+        x, y = S.cfg5()
+        kw, cost = dict(eps=0.01, normalize="mean"), "squared euclidean / mean of 20k sampled pairs"
+    else:
+        raise ValueError(name)
+    cfg = {"workload": name, "n": len(x), "m": len(y), "d": x.shape[1], "eps": kw["eps"], "cost": cost,
+           "l2": L2_NOTE}
+    return x, y, kw, cfg
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# Clocks during the timed region
+# ----------------------------------------------------------------------------------------------------------------
 
 class NvmlClocks:
     """SM clock and throttle-reason samples every ~1 ms through NVML while the timed region runs (the region can be a
@@ -199,317 +236,515 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_oracle_iteration_ms(x, y, kw, max_seconds: float, threads: int | None = None):
-    """The reference's CPU solver (oracle port, torch float32, all threads) on a bounded sample of the workload:
-    whole iterations when they fit the time budget, else the f and g half-steps over a subset of rows, scaled."""
-    from oracle import trnopt_oracle as O
-    torch.set_num_threads(threads or os.cpu_count() or 1)
-    eps = kw["eps"]
-    if kw["normalize"]:
-        center, scale = O.normalization(x, y, how="mean")
-    else:
-        center, scale = np.zeros(x.shape[1]), 1.0
-    xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
-    n, m = len(xs), len(ys)
-    t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32)
-    X, Y = t(xs), t(ys)
-    XT, YT = X.T.contiguous(), Y.T.contiguous()
-    xsq, ysq = t((xs * xs).sum(1)), t((ys * ys).sum(1))
-    la, lb = torch.full((n,), float(-np.log(n))), torch.full((m,), float(-np.log(m)))
-    zx, zy = torch.zeros(n), torch.zeros(m)
-    gh = torch.zeros(m)
-    inv, e, k = (torch.tensor(v, dtype=torch.float32) for v in (1.0 / eps, eps, 1.0))
+# ----------------------------------------------------------------------------------------------------------------
+# The CPU side: the reference's solver (oracle port) on the host cores
+# ----------------------------------------------------------------------------------------------------------------
 
-    blk = max(n, m) if n * m <= 150_000_000 else 4096   # the reference's default block=None where it fits
+class CpuPort:
+    """The reference's CPU half-step (the oracle port of sinkhorn.py:108-119, torch float32, all host threads) on a
+    bounded sample of one workload: whole iterations when two fit the time budget, else the f and g half-steps over
+    whole blocks of rows (`block` rows a call, the reference's block option), scaled to a full iteration."""
 
-    def iteration(rows_x, rows_y):
-        fh = torch.cat([O.half_step(X[s:s + blk], xsq[s:s + blk], zx[s:s + blk], YT, gh, lb, inv, e, k)
-                        for s in range(0, rows_x, blk)])
-        gg = torch.cat([O.half_step(Y[s:s + blk], ysq[s:s + blk], zy[s:s + blk], XT, fh if rows_x == n else zx, la,
-                                    inv, e, k) for s in range(0, rows_y, blk)])
-        return gg
+    def __init__(self, x, y, kw, threads: int | None = None):
+        from oracle import trnopt_oracle as O
+        torch.set_num_threads(threads or os.cpu_count() or 1)
+        self.O = O
+        if kw["normalize"]:
+            center, scale = O.normalization(x, y, how="mean")
+        else:
+            center, scale = np.zeros(x.shape[1]), 1.0
+        xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
+        self.n, self.m, self.d = len(xs), len(ys), x.shape[1]
+        t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float32)
+        self.X, self.Y = t(xs), t(ys)
+        self.XT, self.YT = self.X.T.contiguous(), self.Y.T.contiguous()
+        self.xsq, self.ysq = t((xs * xs).sum(1)), t((ys * ys).sum(1))
+        self.la = torch.full((self.n,), float(-np.log(self.n)))
+        self.lb = torch.full((self.m,), float(-np.log(self.m)))
+        self.zx, self.zy = torch.zeros(self.n), torch.zeros(self.m)
+        self.gh, self.fh = torch.zeros(self.m), torch.zeros(self.n)
+        eps = kw["eps"]
+        self.c = tuple(torch.tensor(v, dtype=torch.float32) for v in (1.0 / eps, eps, 1.0))
+        # the reference's default block=None (one call over all rows) where its score matrix fits a few GB
+        self.block = max(self.n, self.m) if self.n * self.m <= 150_000_000 else 1024
+        self.t_row = None
 
-    t0 = time.perf_counter()
-    iteration(min(n, 4096), min(m, 4096))                     # warm-up on one block of rows each way
-    t_blk = time.perf_counter() - t0
-    est_full = t_blk * (n / min(n, 4096) + m / min(m, 4096)) / 2
-    if est_full * 2 <= max_seconds:
-        reps, frac = 2, 1.0
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            iteration(n, m)
-        dt = (time.perf_counter() - t0) / reps
-        sample = f"{reps} full iterations ({n}x{m}, d {x.shape[1]}) after a 4096-row warm-up"
-    else:
-        frac = max(4096 / max(n, m), min(1.0, max_seconds / (2 * est_full)))
-        rx, ry = max(1, int(n * frac)), max(1, int(m * frac))
-        t0 = time.perf_counter()
-        iteration(rx, ry)
-        dt = (time.perf_counter() - t0) * (n + m) / (rx + ry)
-        sample = f"f and g half-steps over {rx} + {ry} of {n} + {m} rows, scaled to a full iteration"
-    return dt * 1e3, torch.get_num_threads(), sample
+    def _rows(self, rows_x, rows_y):
+        O, blk = self.O, self.block
+        for s in range(0, rows_x, blk):
+            e = min(s + blk, rows_x)
+            O.half_step(self.X[s:e], self.xsq[s:e], self.zx[s:e], self.YT, self.gh, self.lb, *self.c)
+        for s in range(0, rows_y, blk):
+            e = min(s + blk, rows_y)
+            O.half_step(self.Y[s:e], self.ysq[s:e], self.zy[s:e], self.XT, self.fh, self.la, *self.c)
+
+    def iteration_ms(self, max_seconds: float):
+        """(ms per full iteration, threads, sample description)."""
+        if self.t_row is None:                        # one untimed warm-up block each way, and a time estimate
+            b = min(self.block, self.n, self.m)
+            t0 = time.perf_counter()
+            self._rows(b, b)
+            self.t_row = (time.perf_counter() - t0) / (2 * b)
+        est = self.t_row * (self.n + self.m)
+        if 2 * est <= max_seconds:
+            t0 = time.perf_counter()
+            for _ in range(2):
+                self._rows(self.n, self.m)
+            dt = (time.perf_counter() - t0) / 2
+            sample = f"2 full iterations ({self.n}x{self.m}, d {self.d})"
+        else:
+            frac = min(1.0, max_seconds / est)
+            blk = min(self.block, self.n, self.m)
+            rx = max(blk, int(self.n * frac) // blk * blk)
+            ry = max(blk, int(self.m * frac) // blk * blk)
+            t0 = time.perf_counter()
+            self._rows(rx, ry)
+            dt = (time.perf_counter() - t0) * (self.n + self.m) / (rx + ry)
+            sample = (f"f and g half-steps over {rx} + {ry} of {self.n} + {self.m} rows ({blk}-row calls), "
+                      "scaled to a full iteration")
+        return dt * 1e3, torch.get_num_threads(), sample
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    name, x, y, kw, cfg = workload(args.workload, world)
-    budget_per_step = max(0.5, 150.0 / max(1, args.steps + args.warmup))
-    # Each step is one bounded sample of an iteration, timed on the host's cores.
+    name = resolve_workload(args.workload, world)
+    if name not in ("cfg2", "cfg5", "weak"):
+        print(json.dumps({"impl": "reference", "unavailable": f"--impl reference times iteration workloads "
+                          f"(cfg2, cfg5, weak), not {name}"}), flush=True)
+        return
+    x, y, kw, cfg = workload(name, world)
+    cpu = CpuPort(x, y, kw)
+    per_step = max(1.0, 60.0 / max(1, args.steps + args.warmup))
     vals, cores, sample = [], 0, ""
     for i in range(args.warmup + args.steps):
-        ms, cores, sample = cpu_oracle_iteration_ms(x, y, kw, budget_per_step)
+        ms, cores, sample = cpu.iteration_ms(per_step)
         if i >= args.warmup:
             vals.append(ms)
     v = float(np.mean(vals))
     line = {"metric": METRIC, "value": v, "unit": "ms/iter", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False, "scaling": "weak" if name == "weak"
-            else "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "impl": "reference",
-            "config": {"workload": name, **cfg, "l2": "inputs resident in host memory"},
-            "cpu_baseline": {"value": v, "unit": "ms/iter", "cores": cores, "kind": "port", "sample": sample},
+            "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False,
+            "scaling": "weak" if name == "weak" else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded generators in trnopt/synthetic.py)", "impl": "reference", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": "ms/iter", "cores": cores, "kind": "port",
+                             "sample": f"each step: {sample}"},
             "e2e": {"value": v, "unit": "ms/iter", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_pipeline(args, rank, world, dev):
-    """cfg3 / cfg4: wot transport maps through the public API (trnopt.singlecell), wall time per map / pipeline;
-    cfg2conv: one config-2 solve to convergence through sinkhorn()."""
-    from trnopt import Backend, SinkhornOptions, sinkhorn, synthetic
-    from trnopt.singlecell import wot_trajectory, wot_transport_map
-    opts = SinkhornOptions(backend=Backend.preset("cuda-fused", device=str(dev)), cores=world)
-    last = {}
-    def pinned(a):
-        t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
-        t.numpy()[...] = a
-        return t.numpy()
-    if args.workload == "cfg2conv":
-        xc, yc = (pinned(a) for a in synthetic.cfg2())
-        conv = SinkhornOptions(eps=0.1, tol=1e-6, check_every=10, max_iters=20_000, normalize=False,
-                               backend=opts.backend, cores=world)
-        cfg = {"workload": "cfg2conv", "n": 10_000, "m": 10_000, "d": 64, "eps": 0.1, "tol": 1e-6, "check_every": 10,
-               "input": "host float64 arrays in pinned memory, f and g returned to the host"}
-    elif args.workload == "cfg5conv":
-        xc, yc = (pinned(a) for a in synthetic.cfg5())
-        stages = synthetic.cfg5_eps_stages()
-        conv = SinkhornOptions(eps=0.01, eps_stages=stages, stage_max_iters=50, max_iters=400, fixed_iters=True,
-                               normalize="mean", backend=opts.backend, cores=world)
-        cfg = {"workload": "cfg5conv", "n": len(xc), "m": len(yc), "d": 64, "eps": 0.01,
-               "eps_stages": [round(e, 6) for e in stages], "stage_max_iters": 50, "iterations_in_all": 400,
-               "input": "host float64 arrays in pinned memory, f and g returned to the host"}
-    elif args.workload == "cfg3":
-        x0, x1, g = synthetic.cfg3()
-        pairs = [(x0, x1, g)]
-        cfg = {"workload": "cfg3", "n": len(x0), "m": len(x1), "d": 30, "eps": 0.05, "lambda": [1.0, 50.0],
-               "growth_iters": 3, "tol": 1e-8}
-    else:
-        tr = synthetic.cfg4()
-        pairs = [(tr.cohorts[t], tr.cohorts[t + 1], tr.growth[t]) for t in range(len(tr.cohorts) - 1)]
-        cfg = {"workload": "cfg4", "pairs": len(pairs), "cells": int(sum(len(c) for c in tr.cohorts)), "d": 30,
-               "eps": 0.05, "lambda": [1.0, 50.0], "growth_iters": 3, "tol": 1e-8}
+# ----------------------------------------------------------------------------------------------------------------
+# Our arm
+# ----------------------------------------------------------------------------------------------------------------
 
-    kw = dict(eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8, opts=opts)
-
-    def one():
-        if args.workload in ("cfg2conv", "cfg5conv"):
-            r = sinkhorn(xc, yc, opts=conv)
-            last.update(converged=bool(r.converged), error=float(r.error))
-            return r.iterations
-        if args.workload == "cfg4":          # the whole time course through the public pipeline loop
-            return sum(tm.iterations for tm in wot_trajectory(tr.cohorts, None, tr.growth, **kw))
-        return sum(wot_transport_map(x0, x1, g, **kw).iterations for x0, x1, g in pairs)
-
-    for _ in range(args.warmup):
-        one()
-    torch.cuda.synchronize(dev)
-    times, iters = [], 0
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        iters = one()
-        torch.cuda.synchronize(dev)
-        times.append(time.perf_counter() - t0)
-    v = float(np.mean(times))
-    if rank == 0:
-        metric = {"cfg3": "wot transport map seconds", "cfg4": "38-pair pipeline seconds",
-                  "cfg2conv": "config 2 time to convergence seconds",
-                  "cfg5conv": "config 5 eps-staged solve seconds"}[args.workload]
-        line = {"metric": metric,
-                "value": v, "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-                "dtype": "f32", "data": "synthetic (seeded generators in trnopt.synthetic)",
-                "config": {**cfg, "sinkhorn_iterations": iters, "ms_per_iteration": v * 1e3 / max(1, iters), **last},
-                "gpu_launches": 2 * iters}
-        print(json.dumps(line), flush=True)
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    return (json.loads(p.read_text()), "measured") if p.exists() else ({}, "fallback")
 
 
-def run_ours(args, rank, world, dev):
-    import trnopt.sinkhorn  # noqa: F401
-    from trnopt import Backend, SinkhornOptions, _capi, sinkhorn
-    S = sys.modules["trnopt.sinkhorn"]
-    name, x, y, kw, cfg = workload(args.workload, world)
-    eps = kw["eps"]
-    path = S._resolve_path(args.path, x.shape[1])
-    if kw["normalize"]:
-        center, scale = S.normalization(x, y, how="mean")
-    else:
-        center, scale = np.zeros(x.shape[1]), 1.0
-    xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
-    shift = np.concatenate([xs, ys]).mean(axis=0)
-    xi, yi = xs - shift, ys - shift
-    n, m = len(x), len(y)
-    la, lb = np.full(n, -np.log(n)), np.full(m, -np.log(m))
-    X = S._Cloud(xi, la, world, dev)
-    Y = S._Cloud(yi, lb, world, dev)
-    S._prepare_path(path, X, Y)
-    ws = S._workspace(X, Y, world, dev, path)
-    step = S._CudaStep(dev, world, rank, ws, path=path)
-    exchange = S._exchange(args.exchange, path) if world > 1 else "none"
-    peer = None
-    if exchange == "peer":
-        from trnopt import _comm
-        peer = _comm.region(4 * (X.npad + 2 * Y.npad))
-        fh = peer.tensor(0, X.npad)
-        G = [peer.tensor(4 * X.npad, Y.npad), peer.tensor(4 * (X.npad + Y.npad), Y.npad)]
-        G[0].zero_()
-        fh.zero_()
-        peer.arrive()
-    else:
-        G = [torch.zeros(Y.npad, dtype=torch.float32, device=dev) for _ in range(2)]
-        fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
-    tc = path == "tc"
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
-    counter = [0]
+def roofline(n, m, d, world, launch_ms, path, clocks, traffic, traffic_src):
+    """The north star's roofline of one half-step launch (this GPU's rows of one side against the whole other side):
+    the slowest of the exps at the MUFU rate, the useful contraction FLOPs at the pipe's peak and the algorithmic
+    bytes at HBM (plus NVLink when the rows are shared out). Counts use the unpadded n and m."""
+    pk, src = peaks()
+    max_mhz = pk.get("sm_max_mhz", 1965.0)
+    exps = n * m / world
+    flops = 2.0 * n * m * d / world
+    hbm_bytes = (n / world + m) * (4 * d + 12)
+    nvl_bytes = (n / world) * 4 * (world - 1)
+    bf16 = pk.get("bf16_tflops", 1590.0)
+    ffma = SMS * 128 * 2 * max_mhz * 1e6 / 1e12
+    exp_peak = SMS * MUFU_PER_CLK * max_mhz * 1e6
+    hbm = pk.get("hbm_gbs", 6650.0)
+    bounds = {"exp": exps / exp_peak * 1e6,
+              "contraction": flops / ((ffma if path == "ffma" else bf16) * 1e12) * 1e6,
+              "hbm": hbm_bytes / (hbm * 1e9) * 1e6}
+    if world > 1:
+        bounds["nvlink"] = nvl_bytes / 770e9 * 1e6
+    slow = max(bounds, key=bounds.get)
+    launch_s = launch_ms * 1e-3
+    achieved = exps / launch_s
+    mhz = (clocks or {}).get("sm_mhz") or max_mhz
+    roof = {"bound": "exp", "achieved": achieved, "peak": exp_peak, "unit": "exp/s", "frac": round(achieved / exp_peak, 4),
+            "peak_source": f"derived: {SMS} SMs x {MUFU_PER_CLK} ex2/clk (MUFU) x {max_mhz:.0f} MHz max SM clock "
+                           f"({src} sm_max_mhz)",
+            "traffic": traffic, "traffic_source": traffic_src, "algorithmic_bytes": round(hbm_bytes),
+            "kernel": f"half-step ({path})", "launch_us": round(launch_ms * 1e3, 3),
+            "per_launch": {"exps": exps, "useful_flops": flops, "hbm_bytes": hbm_bytes, "nvlink_bytes_out": nvl_bytes},
+            "bounds_us": {k: round(v, 3) for k, v in bounds.items()}, "slowest": slow,
+            "slowest_frac": round(bounds[slow] / (launch_ms * 1e3), 4),
+            "exp_at_sampled_clock": {"clock_mhz": mhz, "frac": round(achieved / (SMS * MUFU_PER_CLK * mhz * 1e6), 4)},
+            "tensor": {"achieved_tflops": round(flops / launch_s / 1e12, 2), "peak_tflops": bf16,
+                       "frac": round(flops / launch_s / 1e12 / bf16, 4), "peak_source": src,
+                       "note": "useful FLOPs 2 n m d (the 3-pass FP16 split is not counted)"}}
+    if path == "ffma":
+        roof["ffma"] = {"achieved_tflops": round(flops / launch_s / 1e12, 2), "peak_tflops": round(ffma, 2)}
+    return roof
 
-    def iteration(ev=None):
-        # one iteration = f half-step then g half-step, through the same run entries the solver uses
-        i = counter[0]
-        counter[0] += 1
+
+class Solver:
+    """Device-resident clouds, potentials and workspace of one iteration workload, and its timed iterations (the same
+    run entries the solver uses: one trnopt_sinkhorn_run call per iteration on one GPU, one
+    trnopt_sinkhorn_run_sharded call with the peer exchange, half-step + all-gather pairs with NCCL)."""
+
+    def __init__(self, x, y, kw, world, rank, dev, path_opt, exchange_opt):
+        import trnopt.sinkhorn  # noqa: F401
+        S = self.S = sys.modules["trnopt.sinkhorn"]
+        from trnopt import _capi
+        self.capi = _capi
+        self.eps, self.world, self.dev = kw["eps"], world, dev
+        self.path = S._resolve_path(path_opt, x.shape[1])
+        if kw["normalize"]:
+            center, scale = S.normalization(x, y, how="mean")
+        else:
+            center, scale = np.zeros(x.shape[1]), 1.0
+        xs, ys = (x - center) / np.sqrt(scale), (y - center) / np.sqrt(scale)
+        shift = np.concatenate([xs, ys]).mean(axis=0)
+        n, m = len(x), len(y)
+        la, lb = np.full(n, -np.log(n)), np.full(m, -np.log(m))
+        X = self.X = S._Cloud(xs - shift, la, world, dev)
+        Y = self.Y = S._Cloud(ys - shift, lb, world, dev)
+        S._prepare_path(self.path, X, Y)
+        self.ws = S._workspace(X, Y, world, dev, self.path)
+        self.step = S._CudaStep(dev, world, rank, self.ws, path=self.path)
+        self.exchange = S._exchange(exchange_opt, self.path) if world > 1 else "none"
+        self.peer = None
+        if self.exchange == "peer":
+            from trnopt import _comm
+            self.peer = _comm.region(4 * (X.npad + 2 * Y.npad))
+            self.fh = self.peer.tensor(0, X.npad)
+            self.G = [self.peer.tensor(4 * X.npad, Y.npad), self.peer.tensor(4 * (X.npad + Y.npad), Y.npad)]
+            self.G[0].zero_()
+            self.fh.zero_()
+            self.peer.arrive()
+        else:
+            self.G = [torch.zeros(Y.npad, dtype=torch.float32, device=dev) for _ in range(2)]
+            self.fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
+        self.i = 0
+
+    def iteration(self, ev=None, stream=None):
+        X, Y, G, fh, eps, c = self.X, self.Y, self.G, self.fh, self.eps, self.capi
+        i = self.i
+        self.i += 1
         if ev is not None:
             ev[0].record(stream)
-        if peer is not None:
-            _capi.sinkhorn_run_sharded(peer.comm, X.packed, X.sq, None, X.log_w, X.npad, X.sexp, Y.packed, Y.sq, None,
-                                       Y.log_w, Y.npad, Y.sexp, X.d, G[0], G[1], fh, i % 2, 1, eps, 1.0, 1.0, ws)
-        elif world > 1:
-            step(X, Y, G[i % 2], eps, 1.0, out=fh)
-            step(Y, X, fh, eps, 1.0, out=G[(i + 1) % 2])
+        if self.peer is not None:
+            c.sinkhorn_run_sharded(self.peer.comm, X.packed, X.sq, None, X.log_w, X.npad, X.sexp, Y.packed, Y.sq,
+                                   None, Y.log_w, Y.npad, Y.sexp, X.d, G[0], G[1], fh, i % 2, 1, eps, 1.0, 1.0,
+                                   self.ws)
+        elif self.world > 1:
+            self.step(X, Y, G[i % 2], eps, 1.0, out=fh)
+            self.step(Y, X, fh, eps, 1.0, out=G[(i + 1) % 2])
         else:
-            _capi.sinkhorn_run(_capi.PATH_TC if tc else _capi.PATH_FFMA, X.packed if tc else X.xT, X.npad, X.sq, None,
-                               X.log_w, X.npad, X.sexp, Y.packed if tc else Y.xT, Y.npad, Y.sq, None, Y.log_w, Y.npad,
-                               Y.sexp, X.d, G[0], G[1], fh, i % 2, 1, eps, 1.0, 1.0, ws)
+            tc = self.path == "tc"
+            c.sinkhorn_run(c.PATH_TC if tc else c.PATH_FFMA, X.packed if tc else X.xT, X.npad, X.sq, None, X.log_w,
+                           X.npad, X.sexp, Y.packed if tc else Y.xT, Y.npad, Y.sq, None, Y.log_w, Y.npad, Y.sexp,
+                           X.d, G[0], G[1], fh, i % 2, 1, eps, 1.0, 1.0, self.ws)
         if ev is not None:
             ev[1].record(stream)
 
-    for _ in range(args.warmup):
-        iteration()
-    torch.cuda.synchronize(dev)
-    steps = []
-    with NvmlClocks(dev.index, enabled=not args.no_clocks and rank == 0) as clk:
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(dev)
-        for _ in range(args.steps):
-            if not args.no_flush:
-                flush.zero_()
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-            iteration(ev)
-            steps.append(ev)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            torch.distributed.barrier()
-    if peer is not None:
-        peer.wait()
-    step_ms = [a.elapsed_time(b) for a, b in steps]
-    total = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(total, op=torch.distributed.ReduceOp.MAX)
-    ms_per_step = float(total.item()) / args.steps
-    clocks = clk.summary() if rank == 0 else None
-    if _capi.device_error_flags():
-        raise RuntimeError("a kernel reported device error flags during the timed region")
+    def timed(self, steps, warmup, flush, clocks_on, world):
+        """Per-step device ms (this rank) and the clock summary of the timed region."""
+        stream = torch.cuda.current_stream()
+        for _ in range(warmup):
+            self.iteration()
+        torch.cuda.synchronize(self.dev)
+        evs = []
+        with NvmlClocks(self.dev.index, enabled=clocks_on) as clk:
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize(self.dev)
+            for _ in range(steps):
+                if flush is not None:
+                    flush.zero_()
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                self.iteration(ev, stream)
+                evs.append(ev)
+            torch.cuda.synchronize(self.dev)
+            if world > 1:
+                torch.distributed.barrier()
+        if self.peer is not None:
+            self.peer.wait()
+            torch.cuda.synchronize(self.dev)
+        if self.capi.device_error_flags():
+            raise RuntimeError("a kernel reported device error flags during the timed region")
+        return [a.elapsed_time(b) for a, b in evs], clk.summary() if clocks_on else None
 
-    # Roofline of the dominant kernel (the fused half-step): per launch, useful FLOPs 2 rows m d, exps rows m. A step
-    # is two launches of it (f then g, the second allowed to start its prologue early), so a launch is half a step.
-    rows_f, rows_g = X.npad // world, Y.npad // world
-    launch_ms = statistics.mean(step_ms) / 2
-    flops = (2.0 * rows_f * Y.npad * X.d + 2.0 * rows_g * X.npad * X.d) / 2
-    exps = (rows_f * Y.npad + rows_g * X.npad) / 2.0
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    bf16 = peaks.get("bf16_tflops", 1590.0)
-    peak_src = "measured" if peaks else "fallback"
-    mhz = (clocks or {}).get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
-    tflops = flops / (launch_ms * 1e-3) / 1e12
-    ffma_peak = SMS * 128 * 2 * mhz * 1e6 / 1e12
-    sfu_rate = exps / (launch_ms * 1e-3)
-    sfu_peak = SMS * 16 * mhz * 1e6
-    traffic = None
-    tfile = ROOT / "profiles" / f"traffic_{path}_{name}.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
-    roof = {"bound": "tensor", "achieved": round(tflops, 2), "peak": bf16, "unit": "TFLOP/s",
-            "frac": round(tflops / bf16, 4), "traffic": traffic, "peak_source": peak_src,
-            "kernel": f"half-step ({path})", "launch_ms": round(launch_ms, 5),
-            "sfu": {"achieved_exp_per_s": sfu_rate, "peak_exp_per_s": sfu_peak, "frac": round(sfu_rate / sfu_peak, 4),
-                    "clock_mhz": mhz}}
-    if path == "ffma":
-        roof["ffma"] = {"achieved_tflops": round(tflops, 2), "peak_tflops": round(ffma_peak, 2),
-                        "frac": round(tflops / ffma_peak, 4)}
-    # The north star's roofline: the slowest of the contraction at its pipe's peak (useful FLOPs), the exps at the
-    # MUFU rate and the algorithmic bytes at the measured HBM copy rate (both clouds once, 4 bytes per coordinate
-    # in FP32 or as an FP16 hi/lo pair, plus the vectors: (n + m)(4d + 12) per launch); frac = that
-    # bound's time over the measured launch time.
-    hbm = peaks.get("hbm_gbs", 6650.0)
-    bounds_us = {"contraction": flops / ((ffma_peak if path == "ffma" else bf16) * 1e12) * 1e6,
-                 "exp": exps / sfu_peak * 1e6,
-                 "hbm": (X.npad + Y.npad) * (4 * X.d + 12) / (hbm * 1e9) * 1e6}
-    slow = max(bounds_us, key=bounds_us.get)
-    roof["slowest_bound"] = {"name": slow, "bound_us": {k: round(v, 3) for k, v in bounds_us.items()},
-                             "launch_us": round(launch_ms * 1e3, 3), "frac": round(bounds_us[slow] / (launch_ms * 1e3), 4)}
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def pinned(a):
+    """A float64 copy of `a` in page-locked host memory, as a caller feeding a GPU solver keeps its inputs."""
+    t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
+    t.numpy()[...] = a
+    return t.numpy()
+
+
+def timed_call(fn, world, dev, warm: int = 1):
+    """Seconds of one call of fn() after `warm` untimed calls, max over ranks (host clock around a synchronised
+    call: these are whole solves through the public API, seconds long)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    out = fn()
+    torch.cuda.synchronize(dev)
+    return max_over_ranks(time.perf_counter() - t0, world, dev), out
+
+
+def solve_cfg2conv(world, dev):
+    from trnopt import Backend, SinkhornOptions, sinkhorn
+    x, y = (pinned(a) for a in synthetic().cfg2())
+    opts = SinkhornOptions(eps=0.1, tol=1e-6, check_every=10, max_iters=20_000, normalize=False, cores=world,
+                           backend=Backend.preset("cuda-fused", device=str(dev)))
+    return lambda: sinkhorn(x, y, opts=opts)
+
+
+def solve_cfg5conv(world, dev):
+    from trnopt import Backend, SinkhornOptions, sinkhorn
+    S = synthetic()
+    x, y = (pinned(a) for a in S.cfg5())
+    opts = SinkhornOptions(eps=0.01, eps_stages=S.cfg5_eps_stages(), stage_max_iters=50, max_iters=400,
+                           fixed_iters=True, normalize="mean", cores=world,
+                           backend=Backend.preset("cuda-fused", device=str(dev)))
+    return lambda: sinkhorn(x, y, opts=opts)
+
+
+def wot_kwargs(world, dev):
+    from trnopt import Backend, SinkhornOptions
+    return dict(eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8,
+                opts=SinkhornOptions(backend=Backend.preset("cuda-fused", device=str(dev)), cores=world))
+
+
+def cpu_ms_per_cell_iteration(cpu_cache, x, y, budget=4.0):
+    """CPU port ms per iteration per n m at a config-3 shaped pair (float32, all host threads)."""
+    if "cfg3" not in cpu_cache:
+        c = CpuPort(x, y, dict(eps=0.05, normalize=False))
+        ms, cores, sample = c.iteration_ms(budget)
+        cpu_cache["cfg3"] = (ms / (len(x) * len(y)), cores, sample)
+    return cpu_cache["cfg3"]
+
+
+def extras_cfg2(world, dev, cpu_ms_cfg2, cpu_on):
+    """The metric's other clauses, measured through the public API on this GPU: config 2 to convergence, config 3's
+    wot map, the 38-pair pipeline, and config 5 (the 262k^2 problem) per iteration and as its 400-iteration staged
+    solve. Each with the CPU port's time for the same iterations (extrapolated from measured ms/iter)."""
+    from trnopt.singlecell import wot_trajectory, wot_transport_map
+    S = synthetic()
+    out, cpu_cache = {}, {}
+
+    secs, r = timed_call(solve_cfg2conv(world, dev), world, dev)
+    out["time_to_convergence"] = {
+        "workload": "cfg2conv: config 2 to tol 1e-6 on the balanced marginal error, checked every 10 iterations",
+        "seconds": secs, "iterations": r.iterations, "error": r.error, "converged": bool(r.converged),
+        "ms_per_iteration": secs * 1e3 / r.iterations,
+        "cpu_port_extrapolated_s": (r.iterations * cpu_ms_cfg2 / 1e3) if cpu_ms_cfg2 else None,
+        "input": "one sinkhorn() call from float64 host arrays in pinned memory; f and g returned to the host"}
+
+    x0, x1, growth = S.cfg3()
+    kw = wot_kwargs(world, dev)
+    secs, tm = timed_call(lambda: wot_transport_map(x0, x1, growth, **kw), world, dev)
+    d3 = {"workload": "cfg3: one wot transport map, 7,355 x 8,962 cells, d 30, median cost, eps 0.05, lambda (1, 50), "
+                      "3 growth iterations, tol 1e-8 (float32 stopping floor 5e-6)",
+          "seconds": secs, "iterations": tm.iterations}
+    if cpu_on:
+        per_nm, cores, sample = cpu_ms_per_cell_iteration(cpu_cache, x0, x1)
+        d3["cpu_port_extrapolated_s"] = tm.iterations * per_nm * len(x0) * len(x1) / 1e3
+        d3["cpu_port"] = {"ms_per_iteration": per_nm * len(x0) * len(x1), "cores": cores, "sample": sample}
+    out["cfg3_map"] = d3
+
+    tr = S.cfg4()
+    secs, maps = timed_call(lambda: wot_trajectory(tr.cohorts, None, tr.growth, **kw), world, dev)
+    its = sum(t.iterations for t in maps)
+    d4 = {"workload": "cfg4: 38 consecutive pairs (39 cohorts, 175k cells) through wot_trajectory, config 3's "
+                      "settings", "seconds": secs, "iterations": its, "solves": 3 * len(maps)}
+    if cpu_on:
+        per_nm = cpu_cache["cfg3"][0]
+        cell_its = sum(t.iterations * len(tr.cohorts[k]) * len(tr.cohorts[k + 1]) for k, t in enumerate(maps))
+        d4["cpu_port_extrapolated_s"] = cell_its * per_nm / 1e3
+        d4["cpu_port_note"] = "sum over pairs of iterations x n m x the config-3 CPU ms per iteration per n m"
+    out["pipeline_38pair"] = d4
+
+    x5, y5, kw5, _ = workload("cfg5", 1)
+    sv = Solver(x5, y5, kw5, 1, 0, dev, "auto", "auto")
+    ms, clk = sv.timed(10, 3, None, True, 1)
+    ms5 = statistics.mean(ms)
+    d5 = {"workload": "cfg5: 262,144^2, d 64, eps 0.01, one GPU (the N = 1 point of the strong-scaling curve)",
+          "ms_per_iter": ms5, "steps": 10, "clocks": clk,
+          "roofline": {k: v for k, v in roofline(len(x5), len(y5), 64, 1, ms5 / 2, sv.path, clk, None, None).items()
+                       if k in ("frac", "bounds_us", "launch_us", "exp_at_sampled_clock")}}
+    del sv
+    secs, r = timed_call(solve_cfg5conv(world, dev), world, dev, warm=0)
+    d5["staged_solve"] = {"seconds": secs, "iterations": r.iterations,
+                          "stage_iters": list(getattr(r, "stage_iters", []) or []),
+                          "note": "eps 1.0 -> 0.01 over 8 geometric values, <= 50 iterations per intermediate value, "
+                                  "400 in all; one sinkhorn() call from pinned float64 host arrays, mean "
+                                  "normalisation and upload included; no warm-up call"}
+    if cpu_on:
+        c5 = CpuPort(x5, y5, kw5)
+        cms, cores, sample = c5.iteration_ms(6.0)
+        d5["cpu_port"] = {"ms_per_iter": cms, "cores": cores, "sample": sample,
+                          "staged_solve_extrapolated_s": cms * r.iterations / 1e3}
+    out["cfg5_1gpu"] = d5
+    return out
+
+
+def parity_sharded(world, rank, dev):
+    """Multi-GPU correctness in the bench line: a 32,768^2 config-5-like solve (20 fixed iterations, eps 0.05, mean
+    cost) with its rows split over every rank, against the same solve on rank 0's GPU alone."""
+    from trnopt import Backend, SinkhornOptions, sinkhorn
+    x, y = synthetic().cfg5(n=32_768)
+    be = Backend.preset("cuda-fused", device=str(dev))
+    o = dict(eps=0.05, max_iters=20, fixed_iters=True, normalize="mean", backend=be)
+    rs = sinkhorn(x, y, opts=SinkhornOptions(cores=world, **o))
+    out = None
+    if rank == 0:
+        r1 = sinkhorn(x, y, opts=SinkhornOptions(cores=1, **o))
+        df, dg = rs.f - r1.f, rs.g - r1.g
+        c = (df.mean() - dg.mean()) / 2
+        out = {"case": "32,768^2, d 64, N(0, I)/8, mean cost, eps 0.05, 20 fixed iterations",
+               "ranks": world, "max_df_over_eps": float(max(np.abs(df - c).max(), np.abs(dg + c).max()) / 0.05),
+               "max_df_over_eps_raw": float(max(np.abs(df).max(), np.abs(dg).max()) / 0.05)}
+    torch.distributed.barrier()
+    return out
+
+
+def run_ours(args, rank, world, dev):
+    from trnopt import Backend, SinkhornOptions, sinkhorn
+    name = resolve_workload(args.workload, world)
+    x, y, kw, cfg = workload(name, world)
+    sv = Solver(x, y, kw, world, rank, dev, args.path, args.exchange)
+    flush = None if args.no_flush else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    step_ms, clocks = sv.timed(args.steps, args.warmup, flush, not args.no_clocks and rank == 0, world)
+    ms_per_step = max_over_ranks(sum(step_ms), world, dev) / args.steps
+
+    tfile = ROOT / "profiles" / f"traffic_{sv.path}_{name}.json"
+    traffic = json.loads(tfile.read_text()).get("bytes_per_launch") if tfile.exists() else None
+    tsrc = f"profiles/{tfile.name} (ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch)" if traffic else None
+    launch_ms = statistics.mean(step_ms) / 2          # a step is two launches of the half-step (f then g)
+    roof = roofline(len(x), len(y), x.shape[1], world, launch_ms, sv.path, clocks, traffic, tsrc)
+    n, m = len(x), len(y)
+    X, Y = sv.X, sv.Y
+    del sv
 
     # End to end through the public API: host arrays in, potentials out, K iterations.
     e2e = None
     if not args.no_e2e:
         opts = SinkhornOptions(max_iters=args.steps, fixed_iters=True, backend=Backend.preset("cuda-fused", device=str(dev)),
-                               cores=world, cuda_path=path, cuda_exchange=args.exchange, **kw)
-        # the clouds in pinned (page-locked) host memory, as a caller feeding a GPU solver keeps them: the upload
-        # inside sinkhorn() is then one DMA per cloud
-        def pinned(a):
-            t = torch.empty(a.shape, dtype=torch.float64, pin_memory=True)
-            t.numpy()[...] = a
-            return t.numpy()
+                               cores=world, cuda_path=args.path, cuda_exchange=args.exchange, **kw)
         xh, yh = pinned(x), pinned(y)
+        warm = SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend, cores=world, cuda_path=args.path,
+                               cuda_exchange=args.exchange, **kw)
         for _ in range(max(1, min(args.warmup, 3))):      # warm-up solves of the same problem, untimed
-            sinkhorn(xh, yh, opts=SinkhornOptions(max_iters=2, fixed_iters=True, backend=opts.backend, cores=world,
-                                                  cuda_path=path, cuda_exchange=args.exchange, **kw))
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(dev)
-        t0 = time.perf_counter()
-        r = sinkhorn(xh, yh, opts=opts)
-        torch.cuda.synchronize(dev)
-        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
-        if world > 1:
-            torch.distributed.all_reduce(dt, op=torch.distributed.ReduceOp.MAX)
+            sinkhorn(xh, yh, opts=warm)
+        secs, r = timed_call(lambda: sinkhorn(xh, yh, opts=opts), world, dev, warm=0)
         h2d = X.h2d_bytes + Y.h2d_bytes                 # x, y and their log weights in float64
         d2h = 8 * (n + m)                                 # f and g in float64
-        e2e = {"value": float(dt.item()) * 1e3 / r.iterations, "unit": "ms/iter",
+        e2e = {"value": secs * 1e3 / r.iterations, "unit": "ms/iter",
                "h2d_bytes_per_step": h2d / r.iterations, "d2h_bytes_per_step": d2h / r.iterations,
-               "note": "one public sinkhorn() call on host float64 arrays (pinned memory) after untimed 2-iteration warm-up calls of "
-                       "the same problem (upload, normalisation, padding, "
+               "note": "one public sinkhorn() call on host float64 arrays (pinned memory) after untimed 2-iteration "
+                       "warm-up calls of the same problem (upload, normalisation, padding, "
                        f"{r.iterations} fixed iterations, f and g back to the host), divided by the iterations"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ms, cores, sample = cpu_oracle_iteration_ms(x, y, kw, 20.0)
+    cpu_on = rank == 0 and world == 1 and not args.no_cpu_baseline
+    if cpu_on and name in ("cfg2", "weak"):
+        ms, cores, sample = CpuPort(x, y, kw).iteration_ms(20.0)
         cpu = {"value": ms, "unit": "ms/iter", "cores": cores, "kind": "port", "sample": sample}
+    elif cpu_on and name == "cfg5":
+        ms, cores, sample = CpuPort(x, y, kw).iteration_ms(10.0)
+        cpu = {"value": ms, "unit": "ms/iter", "cores": cores, "kind": "port", "sample": sample}
+
+    extras = {}
+    if not args.no_extras:
+        if name == "cfg2" and world == 1:
+            extras = extras_cfg2(world, dev, cpu["value"] if cpu else None, cpu_on)
+        elif name == "cfg5":
+            secs, r = timed_call(solve_cfg5conv(world, dev), world, dev, warm=0)
+            extras["time_to_convergence"] = {
+                "workload": "cfg5conv: eps 1.0 -> 0.01 over 8 geometric values, <= 50 iterations per intermediate "
+                            "value, 400 in all, mean-normalised cost; one sinkhorn() call per rank from pinned "
+                            "float64 host arrays (upload and normalisation included), no warm-up call",
+                "seconds": secs, "iterations": r.iterations, "gpus": world,
+                "stage_iters": list(getattr(r, "stage_iters", []) or [])}
+            if world > 1:
+                extras["parity"] = parity_sharded(world, rank, dev)
 
     if rank == 0:
         line = {"metric": METRIC, "value": ms_per_step, "unit": "ms/iter", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": False,
-                "scaling": "strong" if name in ("cfg2", "cfg5") else "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic (seeded generators in trnopt.synthetic)",
-                "config": {"workload": name, **cfg, "path": path, "shards": world, "exchange": exchange,
-                           "l2": "flushed between timed steps (256 MB write)"},
-                "gpu_launches": 2 * args.steps, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks}
+                "scaling": "weak" if name == "weak" else "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded generators in trnopt/synthetic.py)", "config": cfg,
+                "run": {"path": roof["kernel"], "shards": world, "exchange": sv_exchange(world, args),
+                        "launcher": "torchrun" if under_torchrun() else "python"},
+                "gpu_launches": 2 * args.steps, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+                **extras}
+        print(json.dumps(line), flush=True)
+
+
+def sv_exchange(world, args):
+    if world == 1:
+        return "none"
+    return args.exchange if args.exchange != "auto" else "peer (tc path) / nccl (ffma path)"
+
+
+def run_pipeline(args, rank, world, dev):
+    """One whole solve through the public API per step, seconds: cfg3 (one wot map), cfg4 (the 38-pair pipeline),
+    cfg2conv (config 2 to tol 1e-6), cfg5conv (config 5's 400-iteration staged solve)."""
+    from trnopt.singlecell import wot_trajectory, wot_transport_map
+    S = synthetic()
+    last = {}
+    if args.workload == "cfg2conv":
+        fn0 = solve_cfg2conv(world, dev)
+        cfg = {"workload": "cfg2conv", "n": 10_000, "m": 10_000, "d": 64, "eps": 0.1, "tol": 1e-6, "check_every": 10}
+    elif args.workload == "cfg5conv":
+        fn0 = solve_cfg5conv(world, dev)
+        cfg = {"workload": "cfg5conv", "n": 262_144, "m": 262_144, "d": 64, "eps": 0.01,
+               "eps_stages": [round(e, 6) for e in S.cfg5_eps_stages()], "stage_max_iters": 50, "iterations": 400}
+    elif args.workload == "cfg3":
+        x0, x1, g = S.cfg3()
+        kw = wot_kwargs(world, dev)
+        fn0 = lambda: wot_transport_map(x0, x1, g, **kw)
+        cfg = {"workload": "cfg3", "n": len(x0), "m": len(x1), "d": 30, "eps": 0.05, "lambda": [1.0, 50.0],
+               "growth_iters": 3, "tol": 1e-8}
+    else:
+        tr = S.cfg4()
+        kw = wot_kwargs(world, dev)
+        fn0 = lambda: wot_trajectory(tr.cohorts, None, tr.growth, **kw)
+        cfg = {"workload": "cfg4", "pairs": len(tr.cohorts) - 1, "cells": int(sum(len(c) for c in tr.cohorts)),
+               "d": 30, "eps": 0.05, "lambda": [1.0, 50.0], "growth_iters": 3, "tol": 1e-8}
+
+    def one():
+        r = fn0()
+        if isinstance(r, list):
+            return sum(t.iterations for t in r)
+        if hasattr(r, "converged"):
+            last.update(converged=bool(r.converged), error=float(r.error))
+        return r.iterations
+
+    for _ in range(args.warmup):
+        one()
+    times, iters = [], 0
+    for _ in range(args.steps):
+        secs, iters = timed_call(one, world, dev, warm=0)
+        times.append(secs)
+    v = float(np.mean(times))
+    if rank == 0:
+        metric = {"cfg3": "wot transport map seconds", "cfg4": "38-pair pipeline seconds",
+                  "cfg2conv": "config 2 time to convergence seconds",
+                  "cfg5conv": "config 5 eps-staged solve seconds"}[args.workload]
+        line = {"metric": metric, "value": v, "unit": "s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generators in trnopt/synthetic.py)",
+                "config": {**cfg, "sinkhorn_iterations": iters, "ms_per_iteration": v * 1e3 / max(1, iters), **last},
+                "gpu_launches": 2 * iters}
         print(json.dumps(line), flush=True)
 
 
@@ -518,12 +753,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        if world == 1 and args.gpus > 1:
-            raise SystemExit("--gpus N > 1 needs torchrun --nproc-per-node N")
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        raise SystemExit("--gpus N > 1 needs torchrun --nproc-per-node N")
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    sys.path.insert(0, str(ROOT / "trainium-sinkhorn_b200"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:

@@ -24,6 +24,18 @@ Files:
                         the plan's row / column sums, masses_from_potentials
                         (examples/sinkhorn_libs_compare.py:43-56) and the ancestor pull-back
                         (examples/singlecell_figures.py:35-47) for a smooth and a subset-indicator distribution
+  cfg2_full.npz         config 2 at full size (10,000^2, d 64, eps 0.1, raw cost), 100 fixed iterations in float64
+                        and float32, and the float64 plan's row / column sums (chunked, the formula of
+                        transport_plan)
+  cfg2_conv.npz         config 2 run to tol 1e-6 (balanced marginal error, checked every 10): the reference's
+                        float32 run (iterations, error, f, g) and its float64 run
+  cfg3_full.npz         config 3 at full size (7,355 x 8,962, d 30) through wot_transport_map (3 growth iterations):
+                        float64 at tol 1e-8, float64 with the float32 stopping rule (tol 5e-6, stage tol 1e-5) and
+                        float32; masses, potentials, learned growth and the eps / kappa of every half-step
+  cfg5_small.npz        config 5's schedule (N(0, I)/8 clouds, mean-normalised cost, eps 1.0 -> 0.01 over 8 values,
+                        <= 50 iterations per intermediate value, 400 in all) at n = m = 8,192: float32, and float64
+                        with the float32 stage rule (stage tol 1e-5); the eps of every half-step, so the per-stage
+                        iteration counts can be compared
 """
 
 from __future__ import annotations
@@ -240,9 +252,111 @@ def plan_cases():
     np.savez_compressed(HERE / "plan_cases.npz", **out)
 
 
+_CALLS: list = []         # (eps, kappa) of every half-step call of a recording backend
+
+
+def _recording(dtype):
+    """A reference Backend whose compile_fn records the eps and kappa of every half-step call it hands out (the
+    reference calls the step once per block of rows with (x, xsq, off, yT, gh, log_b, inv_eps, eps, kappa)), so
+    that the iterations spent at each eps stage can be read back from a run."""
+    from dataclasses import dataclass
+
+    @dataclass(frozen=True)
+    class Recording(Backend):
+        def compile_fn(self, f):
+            def rec(*args):
+                _CALLS.append((float(args[7]), float(args[8])))
+                return f(*args)
+            return rec
+    return Recording(dtype=dtype)
+
+
+def _plan_sums(x, y, f, g, eps, la=None, lb=None, chunk=64):
+    """Row and column sums of the reference's dense plan (transport_plan, sinkhorn.py:397-403: direct-difference
+    cost in float64, raw coordinates) accumulated over row chunks, so the n x m x d temporary is never formed."""
+    n, m = len(x), len(y)
+    la = np.full(n, -np.log(n)) if la is None else la
+    lb = np.full(m, -np.log(m)) if lb is None else lb
+    rows, cols = np.zeros(n), np.zeros(m)
+    for s in range(0, n, chunk):
+        C = ((x[s:s + chunk, None, :] - y[None, :, :]) ** 2).sum(axis=2)
+        P = np.exp(la[s:s + chunk, None] + lb[None, :] + (f[s:s + chunk, None] + g[None, :] - C) / eps)
+        rows[s:s + chunk] = P.sum(axis=1)
+        cols += P.sum(axis=0)
+    return rows, cols
+
+
+def cfg2_full():
+    x, y = synthetic.cfg2()
+    out = {}
+    for tag, be in (("f64", CPU64), ("f32", CPU32)):
+        t = __import__("time").perf_counter()
+        r = ref_sk.sinkhorn(x, y, opts=ref_sk.SinkhornOptions(eps=0.1, max_iters=100, fixed_iters=True,
+                                                             normalize=False, backend=be))
+        print(f"  cfg2 100 its {tag}: {__import__('time').perf_counter() - t:.0f} s", flush=True)
+        dt = np.float64 if tag == "f64" else np.float32
+        out[f"f_{tag}"], out[f"g_{tag}"] = r.f.astype(dt), r.g.astype(dt)
+    out["row_sum_f64"], out["col_sum_f64"] = _plan_sums(x, y, out["f_f64"], out["g_f64"], 0.1)
+    np.savez_compressed(HERE / "cfg2_full.npz", **out)
+
+
+def cfg2_conv():
+    x, y = synthetic.cfg2()
+    out = {}
+    for tag, be in (("f32", CPU32), ("f64", CPU64)):
+        t = __import__("time").perf_counter()
+        r = ref_sk.sinkhorn(x, y, opts=ref_sk.SinkhornOptions(eps=0.1, tol=1e-6, check_every=10, max_iters=20_000,
+                                                             normalize=False, backend=be))
+        print(f"  cfg2 to tol 1e-6 {tag}: {r.iterations} its, error {r.error:.3g}, "
+              f"{__import__('time').perf_counter() - t:.0f} s", flush=True)
+        dt = np.float64 if tag == "f64" else np.float32
+        out[f"f_{tag}"], out[f"g_{tag}"] = r.f.astype(dt), r.g.astype(dt)
+        out[f"meta_{tag}"] = np.array([r.iterations, r.error, float(r.converged)])
+        np.savez_compressed(HERE / "cfg2_conv.npz", **out)      # the float32 run alone is already useful
+
+
+def cfg3_full():
+    x0, x1, growth = synthetic.cfg3()
+    out = {}
+    runs = (("f64", torch.float64, 1e-8, 1e-6), ("f64c", torch.float64, 5e-6, 1e-5), ("f32", torch.float32, 1e-8, 1e-6))
+    for tag, dt, tol, stol in runs:
+        _CALLS.clear()
+        t = __import__("time").perf_counter()
+        tm = wot_transport_map(x0, x1, growth, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=tol,
+                               stage_tol=stol, opts=ref_sk.SinkhornOptions(backend=_recording(dt)))
+        print(f"  cfg3 {tag}: {tm.iterations} its, {__import__('time').perf_counter() - t:.0f} s", flush=True)
+        r = tm.result
+        st = np.float32 if tag == "f32" else np.float64
+        out[f"{tag}_f"], out[f"{tag}_g"] = r.f.astype(st), r.g.astype(st)
+        out[f"{tag}_row_mass"], out[f"{tag}_col_mass"] = r.row_mass, r.col_mass
+        out[f"{tag}_learned"] = np.stack(tm.learned_growth)
+        out[f"{tag}_meta"] = np.array([tm.iterations, r.iterations, r.error, r.cost_scale])
+        out[f"{tag}_calls"] = np.array(_CALLS)
+        np.savez_compressed(HERE / "cfg3_full.npz", **out)
+
+
+def cfg5_small():
+    x, y = synthetic.cfg5(n=8192)
+    stages = synthetic.cfg5_eps_stages()
+    out = {"eps_stages": np.array(stages)}
+    for tag, dt in (("f32", torch.float32), ("f64c", torch.float64)):
+        _CALLS.clear()
+        t = __import__("time").perf_counter()
+        r = ref_sk.sinkhorn(x, y, opts=ref_sk.SinkhornOptions(
+            eps=0.01, eps_stages=stages, stage_max_iters=50, stage_tol=1e-5, max_iters=400, fixed_iters=True,
+            normalize="mean", backend=_recording(dt)))
+        print(f"  cfg5 8192^2 {tag}: {r.iterations} its, {__import__('time').perf_counter() - t:.0f} s", flush=True)
+        st = np.float32 if tag == "f32" else np.float64
+        out[f"{tag}_f"], out[f"{tag}_g"] = r.f.astype(st), r.g.astype(st)
+        out[f"{tag}_calls"] = np.array(_CALLS)
+        out[f"{tag}_meta"] = np.array([r.iterations, r.cost_scale])
+        out["center"] = r.center
+    np.savez_compressed(HERE / "cfg5_small.npz", **out)
+
+
 if __name__ == "__main__":
     which = sys.argv[1:] or ["half_step_kat", "row_lse_kat", "solver_cases", "cfg1", "normalization", "wot_small",
-                             "plan_cases", "pca_cases"]
+                             "plan_cases", "pca_cases", "cfg2_full", "cfg5_small", "cfg3_full", "cfg2_conv"]
     for w in which:
         print("generating", w, flush=True)
         globals()[w]()

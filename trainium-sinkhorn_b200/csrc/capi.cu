@@ -13,15 +13,14 @@ __device__ int g_error_word;
 
 // Per-device lookups cached once per device (the launch path queries them on every half-step).
 namespace {
-constexpr int kMaxDev = 64;
-int* g_error_ptr[kMaxDev] = {};
-int g_cc_major[kMaxDev] = {};
+int* g_error_ptr[kMaxDevices] = {};
+int g_cc_major[kMaxDevices] = {};
 }  // namespace
 
 int* device_error_word() {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDev) dev = 0;
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
   if (g_error_ptr[dev] == nullptr) {
     int* p = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word) == cudaSuccess) g_error_ptr[dev] = p;
@@ -31,7 +30,7 @@ int* device_error_word() {
 }
 
 int device_cc_major(int dev) {
-  if (dev < 0 || dev >= kMaxDev) return 0;
+  if (dev < 0 || dev >= kMaxDevices) return 0;
   if (g_cc_major[dev] == 0) cudaDeviceGetAttribute(&g_cc_major[dev], cudaDevAttrComputeCapabilityMajor, dev);
   return g_cc_major[dev];
 }
@@ -108,15 +107,22 @@ int ffma_run(LseProblem& p, void* ws, size_t ws_bytes, cudaStream_t stream) {
 
 namespace trnopt {
 
-int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
-                        const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
-                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub) {
+int half_step_tc_check(const void* xpack, const float* xsq, const void* ypack, const float* gh, const float* log_b,
+                       int rows, int m, int d, float eps, float kappa, const float* fh) {
   if (!tc_supported_d(d)) return TRNOPT_ERR_UNSUPPORTED;
   if (!xpack || !ypack || !xsq || !gh || !log_b || !fh || rows < 1 || m < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
   if (!aligned(xpack, 128) || !aligned(ypack, 128)) return TRNOPT_ERR_ALIGNMENT;
   if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (device_cc_major(current_device()) != 10) return TRNOPT_ERR_UNSUPPORTED;
+  return TRNOPT_OK;
+}
+
+int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
+                        const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
+                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub) {
+  int st0 = half_step_tc_check(xpack, xsq, ypack, gh, log_b, rows, m, d, eps, kappa, fh);
+  if (st0 != TRNOPT_OK) return st0;
   const int dev = current_device();
-  if (device_cc_major(dev) != 10) return TRNOPT_ERR_UNSUPPORTED;
   LseProblem p{};
   p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off; p.rows = rows; p.m = m; p.d = d;
   const double inv_eps = 1.0 / (double)eps;

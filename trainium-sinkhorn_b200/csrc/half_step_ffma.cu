@@ -184,22 +184,24 @@ __global__ void __launch_bounds__(FF_THREADS, 2) lse_ffma_kernel(LseProblem p, S
 size_t ffma_smem_bytes(int d) { return (size_t)(3 * d * 128 + 2 * 128) * sizeof(float); }
 
 int ffma_grid(int device, int d, long long units) {
-  static int cached_blocks[129] = {0};
-  static int cached_dev = -1, cached_sms = 0;
-  if (cached_dev != device) {
-    cudaDeviceGetAttribute(&cached_sms, cudaDevAttrMultiProcessorCount, device);
-    for (int i = 0; i <= 128; ++i) cached_blocks[i] = 0;
-    cached_dev = device;
-    // One opt-in for the largest tile (d = 128): the attribute is a ceiling, every launch asks for its own size.
-    cudaFuncSetAttribute(lse_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ffma_smem_bytes(128));
+  // Per device: SM count, the shared-memory opt-in (one for the largest tile, d = 128: the attribute is a ceiling,
+  // every launch asks for its own size) and the resident blocks per SM for each d.
+  static std::atomic<int> sms[kMaxDevices], attr_done[kMaxDevices];
+  static std::atomic<int> blocks_for[kMaxDevices][129];
+  if (device < 0 || device >= kMaxDevices) device = 0;
+  int n_sm = sms[device].load();
+  if (n_sm == 0) {
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device);
+    sms[device].store(n_sm);
   }
-  if (cached_blocks[d] == 0) {
-    const size_t smem = ffma_smem_bytes(d);
-    int blocks = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, lse_ffma_kernel, FF_THREADS, smem);
-    cached_blocks[d] = blocks > 0 ? blocks : 1;
+  smem_attr_once(reinterpret_cast<const void*>(lse_ffma_kernel), (int)ffma_smem_bytes(128), attr_done);
+  int blocks = blocks_for[device][d].load();
+  if (blocks == 0) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, lse_ffma_kernel, FF_THREADS, ffma_smem_bytes(d));
+    blocks = blocks > 0 ? blocks : 1;
+    blocks_for[device][d].store(blocks);
   }
-  long long g = (long long)cached_blocks[d] * cached_sms;
+  long long g = (long long)blocks * (n_sm > 0 ? n_sm : 148);
   return (int)(g < units ? g : units);
 }
 

@@ -9,8 +9,10 @@
 // Limits and sharing:
 //   * The array is kStaticScratchBytes (4 MiB) per GPU, held from the moment the library is loaded on that GPU until
 //     the process exits. Problems whose scratch need (trnopt_workspace_size(rows, m, d, TRNOPT_PATH_TC)) exceeds it
-//     are rejected with TRNOPT_ERR_TOO_LARGE before anything is launched. 4 MiB covers config 2 (10k x 10k needs
-//     about 0.5 MB) and problems up to roughly 100k x 100k.
+//     are rejected with TRNOPT_ERR_TOO_LARGE before anything is enqueued. The need grows with the row tiles and
+//     with the stream-K split, which depends on the GPU's SM count, so the largest problem that fits depends on the
+//     device: on a 148-SM B200, 10k x 10k needs about 0.5 MB and 100k x 100k about 3.2 MB. Callers check
+//     trnopt_workspace_size against trnopt_static_scratch_bytes() on their own device.
 //   * Every call on a GPU uses the same array, which keeps whatever the last call left in it. The counters that must
 //     start at zero are cleared (cudaMemsetAsync on the array, no allocation) at the start of every call. Calls
 //     whose kernels can overlap on the GPU (different streams, or several host threads) race on the array and
@@ -26,7 +28,7 @@
 namespace {
 
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;
-constexpr int kMaxDevices = 64;
+using trnopt::kMaxDevices;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
@@ -59,13 +61,15 @@ size_t trnopt_static_scratch_bytes(void) { return kStaticScratchBytes; }
 int trnopt_half_step_tc_static(const void* xpack, const float* xsq, const float* off, const void* ypack,
                                const float* gh, const float* log_b, int rows, int m, int d, int sx, int sy, float eps,
                                float kappa, float* fh, void* stream) {
-  if (!xpack || !ypack || !xsq || !gh || !log_b || !fh || rows < 1 || m < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
-  if (!trnopt::tc_supported_d(d)) return TRNOPT_ERR_UNSUPPORTED;
+  // Every check that trnopt_half_step_tc makes, before anything is enqueued: a rejected call leaves nothing on the
+  // caller's stream (no stray memset node in a graph the caller is capturing).
+  int st = trnopt::half_step_tc_check(xpack, xsq, ypack, gh, log_b, rows, m, d, eps, kappa, fh);
+  if (st != TRNOPT_OK) return st;
   const size_t need = trnopt_workspace_size(rows, m, d, TRNOPT_PATH_TC);
   if (need == 0) return TRNOPT_ERR_UNSUPPORTED;
   if (need > kStaticScratchBytes) return TRNOPT_ERR_TOO_LARGE;
   void* scratch = nullptr;
-  int st = static_scratch(&scratch);
+  st = static_scratch(&scratch);
   if (st != TRNOPT_OK) return st;
   // The arrival counters (one int per 128-row tile, at the start of the scratch) must start at zero.
   const size_t counters = ((size_t)(rows + 127) / 128 * sizeof(int) + 255) / 256 * 256;

@@ -798,12 +798,9 @@ size_t tc_partial_bytes(const StreamK& sk) { return (size_t)sk.nrt * sk.slots * 
 template <int NKB>
 static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, cudaStream_t stream) {
   using C = TcCfg<NKB>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(half_step_tc_kernel<NKB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<int> attr_done[kMaxDevices];
+  cudaError_t e = smem_attr_once(reinterpret_cast<const void*>(half_step_tc_kernel<NKB>), C::SMEM, attr_done);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.sk.grid);
   cfg.blockDim = dim3(TC_THREADS);

@@ -4,9 +4,29 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace trnopt {
+
+constexpr int kMaxDevices = 64;
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) acts on the calling thread's current device only. `done` holds,
+// per device, the largest size already set for `fn`, so a process that drives several GPUs sets it on each of them.
+inline cudaError_t smem_attr_once(const void* fn, int bytes, std::atomic<int>* done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    int cur = done[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !done[dev].compare_exchange_weak(cur, bytes, std::memory_order_release)) {
+    }
+  }
+  return e;
+}
 
 // FFMA tile path (half_step_ffma.cu)
 size_t ffma_smem_bytes(int d);
@@ -48,6 +68,11 @@ cudaError_t plan_lse_launch(int device, const double* x, int n, const double* y,
 cudaError_t ex2_poly_launch(const float* x, float* out, int n, cudaStream_t stream);
 
 int* device_error_word();
+
+// Argument checks of the tcgen05 half-step (pointers, sizes, 128-byte packed clouds, finite eps > 0 and kappa, a
+// compute capability 10 device); TRNOPT_OK or the status trnopt_half_step_tc returns for them. Enqueues nothing.
+int half_step_tc_check(const void* xpack, const float* xsq, const void* ypack, const float* gh, const float* log_b,
+                       int rows, int m, int d, float eps, float kappa, const float* fh);
 
 // The tcgen05 half-step behind trnopt_half_step_tc, with an optional Publish (capi.cu); returns a TRNOPT status.
 int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,

@@ -129,7 +129,8 @@ cudaError_t median_launch(const double* x, const double* y, const double* sqx, c
   const int two = (N % 2ull) == 0ull;
   const unsigned long long ranks[2] = {two ? N / 2 - 1 : N / 2, N / 2};
   const size_t smem = (size_t)2 * d * MD_TILE * sizeof(double);
-  cudaError_t e = cudaFuncSetAttribute(median_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::atomic<int> attr_done[kMaxDevices];
+  cudaError_t e = smem_attr_once(reinterpret_cast<const void*>(median_hist_kernel), (int)smem, attr_done);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)(((m + MD_TILE - 1) / MD_TILE) * (long long)((n + MD_TILE - 1) / MD_TILE));
   for (int w = 0; w < 1 + two; ++w) {

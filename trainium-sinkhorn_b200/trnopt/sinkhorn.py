@@ -26,7 +26,7 @@ path), or by an NCCL all-gather after each half-step ("nccl").
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -79,6 +79,8 @@ class SinkhornResult:
     cost_scale: float
     row_mass: np.ndarray | None = None
     col_mass: np.ndarray | None = None
+    stage_iters: list = field(default_factory=list)   # eps stages: iterations spent at each stage (the last is the
+                                                        # final eps); an addition to the reference's fields
 
 
 def _use_cuda(opts: SinkhornOptions, d: int) -> None:
@@ -394,7 +396,7 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         err_dev = torch.zeros(1, dtype=torch.float32, device=dev)
         runner = _Runs(step, X, Y, G, fh, peer)
         err, converged, it = float("nan"), False, 0
-        stage, stage_it = 0, 0
+        stage, stage_it, stage_iters = 0, 0, []
         stage_tol = max(opts.stage_tol, 1e-5)              # float32 floors (sinkhorn.py:342-344)
         tol = max(opts.tol, 5e-6) if not balanced else opts.tol
         torch.cuda.synchronize(dev)
@@ -422,6 +424,7 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
                     _capi.max_change(gh_prev, gh_new, Y.n, inv_eps, err_dev)
                     ch = float(err_dev.item())
                     if ch < stage_tol or stage_it >= opts.stage_max_iters:
+                        stage_iters.append(stage_it)
                         stage, stage_it = stage + 1, 0
                 continue
             check = (not opts.fixed_iters and (stages or it > len(sched))
@@ -435,6 +438,8 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
             if check and err < tol:
                 converged = True
                 break
+        if stages:
+            stage_iters.append(stage_it)
         gh = G[it % 2]
         f = (fh[:X.n].to(torch.float64) + X.sq64[:X.n]).cpu().numpy()
         g = (gh[:Y.n].to(torch.float64) + Y.sq64[:Y.n]).cpu().numpy()
@@ -452,7 +457,7 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
     cost = float(np.exp(log_a) @ f + np.exp(log_b) @ g) if balanced else float("nan")
     return SinkhornResult(f=f, g=g, iterations=it, error=err, converged=converged, cost=cost, seconds=seconds,
                           eps=opts.eps, rho=opts.rho, center=center, cost_scale=scale, row_mass=row_mass,
-                          col_mass=col_mass)
+                          col_mass=col_mass, stage_iters=stage_iters)
 
 
 def transport_plan(x, y, res: SinkhornResult, a=None, b=None) -> np.ndarray:
