@@ -134,6 +134,34 @@ int trnopt_sinkhorn_run(int path, const void* x_op, int ldx, const float* xsq, c
                         int n_iter, float eps, float kappa_x, float kappa_y, void* workspace, size_t ws_bytes,
                         void* stream);
 
+/* Solve set-up and tear-down on the device, after one float64 upload per cloud. Replace the host work of the
+ * reference's sinkhorn() around the loop: normalisation arithmetic (sinkhorn.py:268-269), the _Cloud layout
+ * (sinkhorn.py:131-167: padding, squared norms in float64 then cast, PAD_LOG_WEIGHT log weights, weights, row
+ * offsets) and the unshift of the returned potentials (sinkhorn.py:375-376).
+ *
+ * trnopt_cloud_stats: stats (2, 3, d) float64 = for cloud 0 (x, n rows) and cloud 1 (y, m rows) of row-major
+ *   (count, d) float64 points, the per-coordinate sum, min and max. Fixed partition and reduction order (the same
+ *   result on every run). scratch: trnopt_cloud_stats_scratch_bytes(d) bytes, 256-byte aligned, zeroed once; left
+ *   zeroed. d <= 128.
+ * trnopt_prepare_cloud: for point i < n, with u = (pts_i - center) / r and v = u - shift (float64; center and
+ *   shift are HOST arrays of d doubles, read during the call): sq64[i] = |v|^2, vec (4, npad) float32 rows
+ *   [|v|^2, log w_i, w_i, off_i], packed row i = the FP16 [hi | lo] split of v 2^scale_exp (as trnopt_pack_cloud;
+ *   if packed != NULL), xT[k * npad + i] = v_k (if xT != NULL), gh0[i] = |u|^2 - |v|^2 (if gh0 != NULL: the
+ *   reference's starting g = |y|^2 in the shifted frame). log_w NULL = log_w_uniform for every point; off NULL = 0.
+ *   Rows n <= i < npad are padding: zeros, log w = -1e9, w = 0.
+ * trnopt_unshift: out[i] = h[i] + sq[i] in float64, i < n (f = fh + |x|^2).
+ * trnopt_take_error_flags: out[0] = the device error word (as trnopt_device_error_flags reports it), which is
+ *   cleared; asynchronous, so one download can bring potentials and flags back together. */
+size_t trnopt_cloud_stats_scratch_bytes(int d);
+int trnopt_cloud_stats(const double* x, int n, const double* y, int m, int d, double* stats, void* scratch,
+                       size_t scratch_bytes, void* stream);
+int trnopt_prepare_cloud(const double* pts, int n, int d, int npad, const double* center, double r,
+                         const double* shift, int scale_exp, const double* log_w, double log_w_uniform,
+                         const double* off, void* packed, float* xT, float* vec, double* sq64, float* gh0,
+                         void* stream);
+int trnopt_unshift(const float* h, const double* sq, int n, double* out, void* stream);
+int trnopt_take_error_flags(double* out, void* stream);
+
 /* Self-test of the FMA-pipe 2^x used to balance exps between MUFU and the FMA units (no reference counterpart):
  * out[i] = 2^x[i] for n floats, max relative error 2.1e-7 over [-125, 100]. */
 int trnopt_test_ex2_poly(const float* x, float* out, int n, void* stream);

@@ -64,6 +64,11 @@ _SIGS = {
     "trnopt_comm_destroy": (_I, [_P]),
     "trnopt_sinkhorn_run_sharded": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I,
                                          _F, _F, _F, _P, _Z, _P]),
+    "trnopt_cloud_stats_scratch_bytes": (_Z, [_I]),
+    "trnopt_cloud_stats": (_I, [_P, _I, _P, _I, _I, _P, _P, _Z, _P]),
+    "trnopt_prepare_cloud": (_I, [_P, _I, _I, _I, _P, _D, _P, _I, _P, _D, _P, _P, _P, _P, _P, _P, _P]),
+    "trnopt_unshift": (_I, [_P, _P, _I, _P, _P]),
+    "trnopt_take_error_flags": (_I, [_P, _P]),
     "trnopt_plan_rows": (_I, [_P, _I, _P, _I, _I, _P, _P, _P, _P, _D, _P, _I, _P, _P]),
     "trnopt_plan_workspace_size": (_Z, [_I, _I]),
     "trnopt_plan_log_row_sums": (_I, [_P, _I, _P, _I, _I, _P, _P, _P, _P, _D, _P, _P, _Z, _P]),
@@ -269,3 +274,40 @@ def device_error_flags() -> int:
     flags = ctypes.c_int(0)
     check(lib.trnopt_device_error_flags(_stream(), ctypes.byref(flags)), "trnopt_device_error_flags")
     return int(flags.value)
+
+
+def cloud_stats_scratch(d: int, device) -> torch.Tensor:
+    """Scratch of trnopt_cloud_stats, zeroed once (the kernel leaves it zeroed)."""
+    nbytes = int(lib.trnopt_cloud_stats_scratch_bytes(d))
+    if nbytes == 0:
+        raise ValueError(f"cloud statistics support 1 <= d <= 128, not {d}")
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
+def cloud_stats(x: torch.Tensor, y: torch.Tensor, stats: torch.Tensor, scratch: torch.Tensor) -> None:
+    """stats (2, 3, d) float64 <- per-coordinate (sum, min, max) of the float64 clouds x (n, d) and y (m, d)."""
+    n, d = x.shape
+    check(lib.trnopt_cloud_stats(_ptr(x), n, _ptr(y), y.shape[0], d, _ptr(stats), _ptr(scratch), scratch.numel(),
+                                 _stream()), "trnopt_cloud_stats")
+
+
+def prepare_cloud(pts: torch.Tensor, n: int, npad: int, center, r: float, shift, scale_exp: int, log_w, lw_uniform,
+                  off, packed, xT, vec, sq64, gh0) -> None:
+    """One cloud in the half-step layout (trnopt_prepare_cloud); center / shift are host float64 arrays."""
+    import numpy as np
+    d = pts.shape[1]
+    c = np.ascontiguousarray(center, dtype=np.float64)
+    sh = np.ascontiguousarray(shift, dtype=np.float64)
+    check(lib.trnopt_prepare_cloud(_ptr(pts), n, d, npad, c.ctypes.data_as(_P), float(r), sh.ctypes.data_as(_P),
+                                   int(scale_exp), _ptr(log_w), float(lw_uniform), _ptr(off), _ptr(packed),
+                                   _ptr(xT), _ptr(vec), _ptr(sq64), _ptr(gh0), _stream()), "trnopt_prepare_cloud")
+
+
+def unshift(h, sq, n: int, out) -> None:
+    """out[:n] = h[:n] + sq[:n] in float64 (device tensors; out may be a view into a larger buffer)."""
+    check(lib.trnopt_unshift(_ptr(h), _ptr(sq), n, _ptr(out), _stream()), "trnopt_unshift")
+
+
+def take_error_flags(out) -> None:
+    """out[0] <- the device error word (cleared), asynchronously."""
+    check(lib.trnopt_take_error_flags(_ptr(out), _stream()), "trnopt_take_error_flags")

@@ -201,6 +201,108 @@ class _Cloud:
             self.kp = _capi.pack_bytes(1, self.d) // 2
 
 
+class _DeviceCloud:
+    """One cloud in the half-step layout, held in buffers kept between solves of the same shape (_Buffers) and
+    filled on the device by trnopt_prepare_cloud: the same attributes as _Cloud (vec = [|x|^2, log w, w, off] as
+    float32 rows; sq64 the float64 norms; packed FP16 rows on the tensor-core path, xT on the FFMA path)."""
+
+    def __init__(self, n: int, d: int, shards: int, dev: torch.device, path: str):
+        unit = ROW_TILE * shards
+        self.n, self.d, self.shards = n, d, shards
+        self.npad = npad = -(-n // unit) * unit
+        self.pts = torch.empty((n, d), dtype=torch.float64, device=dev)          # upload target
+        self.vec = torch.empty((4, npad), dtype=torch.float32, device=dev)
+        self.sq, self.log_w, self.w, self.off = self.vec[0], self.vec[1], self.vec[2], self.vec[3]
+        self.sq64 = torch.empty(npad, dtype=torch.float64, device=dev)
+        self.zero = torch.zeros(npad, dtype=torch.float32, device=dev)
+        self.lw_dev = torch.empty(n, dtype=torch.float64, device=dev)            # non-uniform log weights
+        self.off_dev = torch.empty(n, dtype=torch.float64, device=dev)
+        self.path = path
+        if path == "tc":
+            self.kp = _capi.pack_bytes(1, d) // 2
+            self.packed = torch.empty(npad * self.kp, dtype=torch.float16, device=dev)
+            self.xT = None
+        else:
+            self.packed, self.xT = None, torch.empty((d, npad), dtype=torch.float32, device=dev)
+        self.sexp, self.h2d_bytes = 0, 0
+
+    def pack(self) -> None:
+        pass
+
+    def upload(self, pts: np.ndarray, log_w: np.ndarray, uniform: bool, off) -> None:
+        """Queue the host float64 arrays' copies (asynchronous from page-locked memory)."""
+        self.pts.copy_(torch.from_numpy(pts), non_blocking=True)
+        self.h2d_bytes = pts.nbytes
+        self.uniform = uniform
+        if not uniform:
+            self.lw_dev.copy_(torch.from_numpy(log_w), non_blocking=True)
+            self.h2d_bytes += log_w.nbytes
+        self.has_off = off is not None
+        if off is not None:
+            self.off_dev.copy_(torch.from_numpy(np.ascontiguousarray(off, dtype=np.float64)), non_blocking=True)
+            self.h2d_bytes += 8 * self.n
+
+    def prepare(self, center, r, shift, lw_uniform: float, gh0=None) -> None:
+        _capi.prepare_cloud(self.pts, self.n, self.npad, center, r, shift, self.sexp,
+                            None if self.uniform else self.lw_dev, lw_uniform, self.off_dev if self.has_off else None,
+                            self.packed, self.xT, self.vec, self.sq64, gh0)
+
+
+class _Buffers:
+    """Device and page-locked host buffers of one problem shape on one device, kept between calls made from the
+    same thread: the uploaded clouds and their layouts, the cloud statistics, the workspace (zeroed once; every
+    launch leaves it zeroed), the potentials, and one download buffer for f, g (and the unbalanced masses' half-steps)
+    and the device error flags."""
+
+    _cache: dict = {}
+    _LIMIT = 4
+
+    @classmethod
+    def get(cls, dev, n, m, d, shards, path):
+        import threading
+        key = (dev.index, n, m, d, shards, path, threading.get_ident())
+        b = cls._cache.pop(key, None)
+        if b is None:
+            b = cls(dev, n, m, d, shards, path)
+        cls._cache[key] = b                                 # most recently used last
+        while len(cls._cache) > cls._LIMIT:
+            cls._cache.pop(next(iter(cls._cache)))
+        return b
+
+    @classmethod
+    def drop(cls, b) -> None:
+        for k, v in list(cls._cache.items()):
+            if v is b:
+                del cls._cache[k]
+
+    def __init__(self, dev, n, m, d, shards, path):
+        self.X = _DeviceCloud(n, d, shards, dev, path)
+        self.Y = _DeviceCloud(m, d, shards, dev, path)
+        self.stats = torch.empty((2, 3, d), dtype=torch.float64, device=dev)
+        self.stats_host = torch.empty((2, 3, d), dtype=torch.float64, pin_memory=True)
+        self.stats_scratch = _capi.cloud_stats_scratch(d, dev)
+        code = _capi.PATH_TC if path == "tc" else _capi.PATH_FFMA
+        need = max(_capi.workspace_size(self.X.npad // shards, self.Y.npad, d, code),
+                   _capi.workspace_size(self.Y.npad // shards, self.X.npad, d, code))
+        self.ws = _capi.new_workspace(need, dev)
+        self.G = [torch.empty(self.Y.npad, dtype=torch.float32, device=dev) for _ in range(2)]
+        self.fh = torch.empty(self.X.npad, dtype=torch.float32, device=dev)
+        self.hb = torch.empty(max(self.X.npad, self.Y.npad), dtype=torch.float32, device=dev)
+        self.out = torch.empty(2 * (n + m) + 1, dtype=torch.float64, device=dev)
+        self.out_host = torch.empty(2 * (n + m) + 1, dtype=torch.float64, pin_memory=True)
+        self.err = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def frame(self, center: np.ndarray, r: float) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """After the statistics are on the host: the internal frame's translation (the joint mean of the
+        normalised clouds) and each cloud's largest |coordinate| in that frame, with the kernel's arithmetic."""
+        st = self.stats_host.numpy()
+        n, m = self.X.n, self.Y.n
+        shift = ((st[0, 0] - n * center) / r + (st[1, 0] - m * center) / r) / (n + m)
+        mx = [max(np.abs((st[c, 2] - center) / r - shift).max(), np.abs((st[c, 1] - center) / r - shift).max())
+              for c in (0, 1)]
+        return shift, mx[0], mx[1]
+
+
 class _CudaStep:
     """A half-step with the fused kernel: this rank's share of the rows of `side` against all of `other`, then
     (P > 1) an all-gather so every rank holds the whole new shifted potential. The counterpart of the reference's
@@ -347,21 +449,24 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         center, scale = np.zeros(x.shape[1]), 1.0
 
     with torch.cuda.device(dev):
-        # One float64 upload per cloud; the normalisation (sinkhorn.py:268-269) and the internal frame (joint mean at
-        # the origin) in float64 on the device.
-        xd = torch.as_tensor(x).to(dev)
-        yd = torch.as_tensor(y).to(dev)
-        c = torch.as_tensor(np.asarray(center, dtype=np.float64)).to(dev)
+        # One float64 upload per cloud into buffers kept for this shape; the per-coordinate statistics on the device
+        # (one small download and the call's one mid-way synchronisation) give the internal frame (the normalised
+        # clouds' joint mean at the origin) and the FP16 split scales; then each cloud's layout (the reference's
+        # _Cloud, sinkhorn.py:131-167, after the normalisation of :268-269) is written by one kernel.
+        path = _resolve_path(opts.cuda_path, x.shape[1])
+        B = _Buffers.get(dev, len(x), len(y), x.shape[1], shards, path)
+        X, Y = B.X, B.Y
+        ua, ub = a is None, b is None
+        X.upload(np.ascontiguousarray(x), log_a, ua, off_x)
+        Y.upload(np.ascontiguousarray(y), log_b, ub, off_y)
+        _capi.cloud_stats(X.pts, Y.pts, B.stats, B.stats_scratch)
+        B.stats_host.copy_(B.stats, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
         r = float(np.sqrt(scale))
-        xs, ys = (xd - c) / r, (yd - c) / r
-        shift = torch.cat([xs, ys]).mean(dim=0)
-        xi, yi = xs - shift, ys - shift
-        X = _Cloud(xi, log_a, shards, dev, off_x)
-        Y = _Cloud(yi, log_b, shards, dev, off_y)
-        path = _resolve_path(opts.cuda_path, X.d)
-        _prepare_path(path, X, Y)
-        ws = _workspace(X, Y, shards, dev, path)
-        step = _CudaStep(dev, shards, rank, ws, group, path)
+        center = np.asarray(center, dtype=np.float64)
+        shift, mx, my = B.frame(center, r)
+        X.sexp, Y.sexp = _scale_exp(mx), _scale_exp(my)
+        step = _CudaStep(dev, shards, rank, B.ws, group, path)
 
         sched = []
         stages = [e for e in (opts.eps_stages or ()) if e > opts.eps]
@@ -374,32 +479,28 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         def kap(e, rho):
             return 1.0 if rho is None else rho / (rho + e)
 
-        # The reference starts from gh = 0 in its frame, i.e. g = |ys|^2; in the internal frame that is
-        # gh = |ys|^2 - |yi|^2 (exactly the same iteration).
-        gh0 = torch.zeros(Y.npad, dtype=torch.float64, device=dev)
-        gh0[:Y.n] = (ys * ys).sum(dim=1) - (yi * yi).sum(dim=1)
-        del xd, yd, xs, ys, xi, yi
-        # Ping-pong potentials: before iteration i the shifted g is G[i % 2]; fh has one buffer.
+        # Ping-pong potentials: before iteration i the shifted g is G[i % 2]; fh has one buffer. The reference starts
+        # from gh = 0 in its frame, i.e. g = |ys|^2; in the internal frame that is gh = |ys|^2 - |yi|^2 (exactly the
+        # same iteration), written into G[0] by Y's layout kernel.
         peer = None
         if shards > 1 and _exchange(opts.cuda_exchange, path) == "peer":
             from . import _comm
             peer = _comm.region(4 * (X.npad + 2 * Y.npad), group)
             fh = peer.tensor(0, X.npad)
             G = [peer.tensor(4 * X.npad, Y.npad), peer.tensor(4 * (X.npad + Y.npad), Y.npad)]
-            G[0].copy_(torch.as_tensor(gh0, dtype=torch.float32))
-            fh.zero_()
-            peer.arrive()                                  # the others may write into these buffers from here on
         else:
-            G = [torch.as_tensor(gh0, dtype=torch.float32).to(dev),
-                 torch.empty(Y.npad, dtype=torch.float32, device=dev)]
-            fh = torch.zeros(X.npad, dtype=torch.float32, device=dev)
-        err_dev = torch.zeros(1, dtype=torch.float32, device=dev)
+            G, fh = B.G, B.fh
+        X.prepare(center, r, shift, log_a[0])
+        Y.prepare(center, r, shift, log_b[0], gh0=G[0])
+        fh.zero_()
+        if peer is not None:
+            peer.arrive()                                  # the others may write into these buffers from here on
+        err_dev = B.err
         runner = _Runs(step, X, Y, G, fh, peer)
         err, converged, it = float("nan"), False, 0
         stage, stage_it, stage_iters = 0, 0, []
         stage_tol = max(opts.stage_tol, 1e-5)              # float32 floors (sinkhorn.py:342-344)
         tol = max(opts.tol, 5e-6) if not balanced else opts.tol
-        torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         while it < opts.max_iters:
             # The loop of sinkhorn.py:346-378, advanced a run of iterations at a time: a run ends where the host
@@ -441,18 +542,33 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         if stages:
             stage_iters.append(stage_it)
         gh = G[it % 2]
-        f = (fh[:X.n].to(torch.float64) + X.sq64[:X.n]).cpu().numpy()
-        g = (gh[:Y.n].to(torch.float64) + Y.sq64[:Y.n]).cpu().numpy()
-        row_mass = col_mass = None
+        # Unshift on the device into one float64 buffer (f, g, and for unbalanced the balanced half-steps' fb, gb),
+        # the error flags at its end, one download (sinkhorn.py:375-389).
+        nx, ny = X.n, Y.n
+        out = B.out
+        _capi.unshift(fh, X.sq64, nx, out)
+        _capi.unshift(gh, Y.sq64, ny, _Off(out, nx, 8))
         if not balanced:
             # The plan's marginals from one balanced (kappa = 1, no offset) update each way (sinkhorn.py:381-389).
-            fb = (step(X, Y, gh, opts.eps, 1.0, use_off=False)[:X.n].to(torch.float64) + X.sq64[:X.n]).cpu().numpy()
-            gb = (step(Y, X, fh, opts.eps, 1.0, use_off=False)[:Y.n].to(torch.float64) + Y.sq64[:Y.n]).cpu().numpy()
+            hx = step(X, Y, gh, opts.eps, 1.0, use_off=False, out=B.hb[:X.npad])
+            _capi.unshift(hx, X.sq64, nx, _Off(out, nx + ny, 8))
+            hy = step(Y, X, fh, opts.eps, 1.0, use_off=False, out=B.hb[:Y.npad])
+            _capi.unshift(hy, Y.sq64, ny, _Off(out, 2 * nx + ny, 8))
+        total = 2 * (nx + ny) + 1
+        _capi.take_error_flags(_Off(out, total - 1, 8))
+        B.out_host[:total].copy_(out[:total], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        host = B.out_host.numpy()
+        flags = int(host[total - 1])
+        if flags:
+            _Buffers.drop(B)                                # its workspace may hold a stopped launch's counters
+            raise _capi.TrnoptError(f"a kernel reported device error flags {flags:#x} during the solve")
+        f, g = host[:nx].copy(), host[nx:nx + ny].copy()
+        row_mass = col_mass = None
+        if not balanced:
+            fb, gb = host[nx + ny:2 * nx + ny], host[2 * nx + ny:2 * (nx + ny)]
             row_mass = np.exp(log_a + (f - fb) / opts.eps)
             col_mass = np.exp(log_b + (g - gb) / opts.eps)
-        flags = _capi.device_error_flags()
-        if flags:
-            raise _capi.TrnoptError(f"a kernel reported device error flags {flags:#x} during the solve")
         seconds = time.perf_counter() - t0
     cost = float(np.exp(log_a) @ f + np.exp(log_b) @ g) if balanced else float("nan")
     return SinkhornResult(f=f, g=g, iterations=it, error=err, converged=converged, cost=cost, seconds=seconds,
