@@ -121,6 +121,15 @@ int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float*
                           float* out, void* stream);
 int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream);
 
+/* Balanced solves only: move the potential gh (npad entries, the first n real) by K = its mean over the n real
+ * entries rounded to float32, gh -= K, and add K to gauge[0] (float64, device). The plan and, in exact arithmetic,
+ * the iteration are unchanged by a constant c in (f + c, g - c) (the balanced problem's gauge freedom, which the
+ * reference's loop carries from its start g = |y|^2); keeping the stored potentials near zero keeps float32's
+ * absolute precision on them. The caller puts the offset back (trnopt_unshift with sign +1 for g, -1 for f).
+ * state: NULL, or a TrnoptSolveState (below) whose done flag makes the call return at once.
+ * No reference counterpart (the reference's float64 path does not need it). */
+int trnopt_recenter(float* gh, int n, int npad, double* gauge, const void* state, void* stream);
+
 /* n_iter Sinkhorn iterations in one call: for i < n_iter, with g = (start_parity + i) odd ? g1 : g0 and the other
  * buffer g',  fh <- half_step(x side, y side, g, kappa_x);  g' <- half_step(y side, x side, fh, kappa_y),
  * i.e. the body of the reference's loop, sweep(Xs, Ys, ...) then sweep(Ys, Xs, ...) (sinkhorn.py:353-354),
@@ -149,7 +158,8 @@ int trnopt_sinkhorn_run(int path, const void* x_op, int ldx, const float* xsq, c
  *   if packed != NULL), xT[k * npad + i] = v_k (if xT != NULL), gh0[i] = |u|^2 - |v|^2 (if gh0 != NULL: the
  *   reference's starting g = |y|^2 in the shifted frame). log_w NULL = log_w_uniform for every point; off NULL = 0.
  *   Rows n <= i < npad are padding: zeros, log w = -1e9, w = 0.
- * trnopt_unshift: out[i] = h[i] + sq[i] in float64, i < n (f = fh + |x|^2).
+ * trnopt_unshift: out[i] = (h[i] + sq[i]) + sign * gauge[0] in float64, i < n (f = fh + |x|^2, with the offset
+ *   that trnopt_recenter took out of a balanced solve's potentials put back; gauge NULL = 0; sign +1 or -1).
  * trnopt_take_error_flags: out[0] = the device error word (as trnopt_device_error_flags reports it), which is
  *   cleared; asynchronous, so one download can bring potentials and flags back together. */
 size_t trnopt_cloud_stats_scratch_bytes(int d);
@@ -159,8 +169,46 @@ int trnopt_prepare_cloud(const double* pts, int n, int d, int npad, const double
                          const double* shift, int scale_exp, const double* log_w, double log_w_uniform,
                          const double* off, void* packed, float* xT, float* vec, double* sq64, float* gh0,
                          void* stream);
-int trnopt_unshift(const float* h, const double* sq, int n, double* out, void* stream);
+int trnopt_unshift(const float* h, const double* sq, int n, const double* gauge, int sign, double* out,
+                   void* stream);
 int trnopt_take_error_flags(double* out, void* stream);
+
+/* The solver loop decided on the GPU. The reference's loop (sinkhorn.py:346-378) looks at the potentials every
+ * check_every iterations on the host: the balanced marginal error or the maximum potential change, a move to the
+ * next eps stage, convergence. Here that state lives in device memory and a check kernel applies the same rules
+ * after each run of iterations, so the host can queue many runs and read the state once:
+ *   trnopt_solve_init          fill a TrnoptSolveState (device memory, sizeof(TrnoptSolveState) bytes, 8-byte
+ *                              aligned) with the plan and the loop's starting counters (it0: iterations already run,
+ *                              e.g. an eps-scaling prefix; the stage counter starts equal to it). Synchronous copy.
+ *   trnopt_sinkhorn_run_checked
+ *                              trnopt_sinkhorn_run with eps and the kappas of the state's current stage, then the
+ *                              check for the run's end (n_iter must end at a check point: it0 + iterations run so
+ *                              far + n_iter a multiple of check_every, or max_iters). w_y: the y side's weights
+ *                              (npad entries, 0 on padding) for the balanced error. Once the state is done
+ *                              (converged, or max_iters reached) every later half-step, check and recentring
+ *                              returns at once, leaving the potentials of the converged iteration in place.
+ * The fields below `it` are the loop's counters and result (read them from a copy of the struct on the host):
+ * it = iterations, converged, err = the last check's value, stage_iters[k] = iterations spent at intermediate stage
+ * k (k < stage). No reference counterpart as an interface: it restates the reference loop's decisions. */
+#define TRNOPT_MAX_STAGES 32
+typedef struct TrnoptSolveState {
+  double stage_eps[TRNOPT_MAX_STAGES + 1]; /* intermediate eps values, then the final eps at [n_stages] */
+  double rho[2];                           /* marginal penalties of the x and y sides; < 0: balanced (kappa 1) */
+  float tol, stage_tol;                    /* as the reference clamps them for float32 (sinkhorn.py:342-344) */
+  int n_stages, check_every, max_iters, stage_max_iters, fixed_iters, balanced, sched_len, n_real, npad;
+  float eps, kappa[2], dot2, gh2;          /* the current stage's half-step parameters (float, as a host call) */
+  int it, stage, stage_it, done, converged;
+  float err;
+  int stage_iters[TRNOPT_MAX_STAGES + 1];
+} TrnoptSolveState;
+int trnopt_solve_init(void* state, const double* stage_eps, int n_stages, double final_eps, double rho_x,
+                      double rho_y, int check_every, int max_iters, int stage_max_iters, int fixed_iters,
+                      int sched_len, float tol, float stage_tol, int n_real, int npad, int it0, void* stream);
+int trnopt_sinkhorn_run_checked(int path, const void* x_op, int ldx, const float* xsq, const float* xoff,
+                                const float* log_a, int nx, int sx, const void* y_op, int ldy, const float* ysq,
+                                const float* yoff, const float* log_b, int ny, int sy, int d, float* g0, float* g1,
+                                float* fh, int start_parity, int n_iter, void* state, const float* w_y,
+                                void* workspace, size_t ws_bytes, void* stream);
 
 /* Self-test of the FMA-pipe 2^x used to balance exps between MUFU and the FMA units (no reference counterpart):
  * out[i] = 2^x[i] for n floats, max relative error 2.1e-7 over [-125, 100]. */

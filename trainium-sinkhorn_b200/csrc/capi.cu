@@ -119,7 +119,8 @@ int half_step_tc_check(const void* xpack, const float* xsq, const void* ypack, c
 
 int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
                         const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
-                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub) {
+                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub,
+                        const TrnoptSolveState* dyn, int side, bool pdl) {
   int st0 = half_step_tc_check(xpack, xsq, ypack, gh, log_b, rows, m, d, eps, kappa, fh);
   if (st0 != TRNOPT_OK) return st0;
   const int dev = current_device();
@@ -130,12 +131,35 @@ int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, c
   p.gh2 = (float)(inv_eps * 1.4426950408889634);
   p.lb2 = kLog2e;
   p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
+  p.dyn = dyn; p.side = side;
   StreamK sk{};
   tc_plan(dev, rows, m, d, sk);
   int st = bind_workspace(sk, tc_partial_bytes(sk), workspace, ws_bytes);
   if (st != TRNOPT_OK) return st;
   p.error_word = device_error_word();
-  return cuda_status(tc_launch(p, xpack, ypack, sx, sy, sk, stream, pub));
+  return cuda_status(tc_launch(p, xpack, ypack, sx, sy, sk, stream, pub, pdl));
+}
+
+int half_step_ffma_launch(const float* xT, int ldx, const float* xsq, const float* off, const float* yT, int ldy,
+                          const float* gh, const float* log_b, int rows, int m, int d, float eps, float kappa, float* fh,
+                          void* workspace, size_t ws_bytes, cudaStream_t stream, const TrnoptSolveState* dyn,
+                          int side) {
+  if (d > 128) return TRNOPT_ERR_UNSUPPORTED;
+  int st = check_points(xT, ldx, rows, d);
+  if (st == TRNOPT_OK) st = check_points(yT, ldy, m, d);
+  if (st != TRNOPT_OK) return st;
+  if (xsq == nullptr || gh == nullptr || log_b == nullptr || fh == nullptr) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  LseProblem p{};
+  p.xT = xT; p.ldx = ldx; p.yT = yT; p.ldy = ldy; p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off;
+  p.rows = rows; p.m = m; p.d = d;
+  const double inv_eps = 1.0 / (double)eps;
+  p.dot2 = (float)(2.0 * inv_eps * 1.4426950408889634);
+  p.gh2 = (float)(inv_eps * 1.4426950408889634);
+  p.lb2 = kLog2e;
+  p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
+  p.dyn = dyn; p.side = side;
+  return ffma_run(p, workspace, ws_bytes, stream);
 }
 
 }  // namespace trnopt
@@ -201,21 +225,8 @@ int trnopt_workspace_init(void* workspace, size_t ws_bytes, void* stream) {
 int trnopt_half_step(const float* xT, int ldx, const float* xsq, const float* off, const float* yT, int ldy,
                      const float* gh, const float* log_b, int rows, int m, int d, float eps, float kappa, float* fh,
                      void* workspace, size_t ws_bytes, void* stream) {
-  if (d > 128) return TRNOPT_ERR_UNSUPPORTED;
-  int st = check_points(xT, ldx, rows, d);
-  if (st == TRNOPT_OK) st = check_points(yT, ldy, m, d);
-  if (st != TRNOPT_OK) return st;
-  if (xsq == nullptr || gh == nullptr || log_b == nullptr || fh == nullptr) return TRNOPT_ERR_INVALID_ARGUMENT;
-  if (!(eps > 0.f) || !isfinite(eps) || !isfinite(kappa)) return TRNOPT_ERR_INVALID_ARGUMENT;
-  LseProblem p{};
-  p.xT = xT; p.ldx = ldx; p.yT = yT; p.ldy = ldy; p.gh = gh; p.log_b = log_b; p.xsq = xsq; p.off = off;
-  p.rows = rows; p.m = m; p.d = d;
-  const double inv_eps = 1.0 / (double)eps;
-  p.dot2 = (float)(2.0 * inv_eps * 1.4426950408889634);
-  p.gh2 = (float)(inv_eps * 1.4426950408889634);
-  p.lb2 = kLog2e;
-  p.eps = (double)eps; p.kappa = (double)kappa; p.mode = 0; p.out = fh;
-  return ffma_run(p, workspace, ws_bytes, reinterpret_cast<cudaStream_t>(stream));
+  return half_step_ffma_launch(xT, ldx, xsq, off, yT, ldy, gh, log_b, rows, m, d, eps, kappa, fh, workspace, ws_bytes,
+                               reinterpret_cast<cudaStream_t>(stream), nullptr, 0);
 }
 
 int trnopt_row_lse(const float* xaT, int ldx, const float* yaT, int ldy, int rows, int m, int k, float* lse,
@@ -268,11 +279,12 @@ int trnopt_sinkhorn_run(int path, const void* x_op, int ldx, const float* xsq, c
     float* gn = ((start_parity + i) & 1) ? g0 : g1;
     int st;
     if (path == TRNOPT_PATH_TC) {
-      st = trnopt_half_step_tc(x_op, xsq, xoff, y_op, gc, log_b, nx, ny, d, sx, sy, eps, kappa_x, fh, workspace,
-                               ws_bytes, stream);
+      cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+      st = half_step_tc_launch(x_op, xsq, xoff, y_op, gc, log_b, nx, ny, d, sx, sy, eps, kappa_x, fh, workspace,
+                               ws_bytes, s, nullptr, nullptr, 0, true);
       if (st == TRNOPT_OK)
-        st = trnopt_half_step_tc(y_op, ysq, yoff, x_op, fh, log_a, ny, nx, d, sy, sx, eps, kappa_y, gn, workspace,
-                                 ws_bytes, stream);
+        st = half_step_tc_launch(y_op, ysq, yoff, x_op, fh, log_a, ny, nx, d, sy, sx, eps, kappa_y, gn, workspace,
+                                 ws_bytes, s, nullptr, nullptr, 1, true);
     } else if (path == TRNOPT_PATH_FFMA) {
       const float* xT = static_cast<const float*>(x_op);
       const float* yT = static_cast<const float*>(y_op);
@@ -305,6 +317,86 @@ int trnopt_balanced_error(const float* gh_old, const float* gh_new, const float*
                           float* out, void* stream) {
   if (!gh_old || !gh_new || !w || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
   return cuda_status(balanced_error_launch(gh_old, gh_new, w, n, inv_eps, out, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_recenter(float* gh, int n, int npad, double* gauge, const void* state, void* stream) {
+  if (!gh || !gauge || n < 1 || npad < n) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned(gauge, 8) || !aligned(state, 8)) return TRNOPT_ERR_ALIGNMENT;
+  return cuda_status(recenter_launch(gh, n, npad, gauge, static_cast<const TrnoptSolveState*>(state),
+                                     reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_solve_init(void* state, const double* stage_eps, int n_stages, double final_eps, double rho_x,
+                      double rho_y, int check_every, int max_iters, int stage_max_iters, int fixed_iters,
+                      int sched_len, float tol, float stage_tol, int n_real, int npad, int it0, void* stream) {
+  if (!state || n_stages < 0 || n_stages > TRNOPT_MAX_STAGES || (n_stages > 0 && !stage_eps)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!(final_eps > 0.0) || check_every < 1 || max_iters < 0 || n_real < 1 || npad < n_real || it0 < 0)
+    return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned(state, 8)) return TRNOPT_ERR_ALIGNMENT;
+  TrnoptSolveState h{};
+  for (int k = 0; k < n_stages; ++k) {
+    if (!(stage_eps[k] > 0.0)) return TRNOPT_ERR_INVALID_ARGUMENT;
+    h.stage_eps[k] = stage_eps[k];
+  }
+  h.stage_eps[n_stages] = final_eps;
+  h.rho[0] = rho_x;
+  h.rho[1] = rho_y;
+  h.tol = tol;
+  h.stage_tol = stage_tol;
+  h.n_stages = n_stages;
+  h.check_every = check_every;
+  h.max_iters = max_iters;
+  h.stage_max_iters = stage_max_iters;
+  h.fixed_iters = fixed_iters;
+  h.balanced = rho_x < 0.0 && rho_y < 0.0;
+  h.sched_len = sched_len;
+  h.n_real = n_real;
+  h.npad = npad;
+  h.it = it0;
+  h.stage_it = it0;
+  h.done = it0 >= max_iters;
+  h.err = nanf("");                  // no check yet
+  solve_stage_params(h);
+  return cuda_status(cudaMemcpyAsync(state, &h, sizeof(h), cudaMemcpyHostToDevice,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int trnopt_sinkhorn_run_checked(int path, const void* x_op, int ldx, const float* xsq, const float* xoff,
+                                const float* log_a, int nx, int sx, const void* y_op, int ldy, const float* ysq,
+                                const float* yoff, const float* log_b, int ny, int sy, int d, float* g0, float* g1,
+                                float* fh, int start_parity, int n_iter, void* state, const float* w_y,
+                                void* workspace, size_t ws_bytes, void* stream) {
+  if (n_iter < 1 || !g0 || !g1 || !fh || !state || !w_y) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned(state, 8)) return TRNOPT_ERR_ALIGNMENT;
+  const TrnoptSolveState* dyn = static_cast<const TrnoptSolveState*>(state);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // eps and kappa come from the state; the values given here only pass the argument checks
+  const float eps = 1.0f, kappa = 1.0f;
+  for (int i = 0; i < n_iter; ++i) {
+    float* gc = ((start_parity + i) & 1) ? g1 : g0;
+    float* gn = ((start_parity + i) & 1) ? g0 : g1;
+    int st;
+    if (path == TRNOPT_PATH_TC) {
+      // the run's first half-step follows the previous check without overlap, so it sees the state that check wrote
+      st = half_step_tc_launch(x_op, xsq, xoff, y_op, gc, log_b, nx, ny, d, sx, sy, eps, kappa, fh, workspace, ws_bytes,
+                               s, nullptr, dyn, 0, i > 0);
+      if (st == TRNOPT_OK)
+        st = half_step_tc_launch(y_op, ysq, yoff, x_op, fh, log_a, ny, nx, d, sy, sx, eps, kappa, gn, workspace,
+                                 ws_bytes, s, nullptr, dyn, 1, true);
+    } else if (path == TRNOPT_PATH_FFMA) {
+      const float* xT = static_cast<const float*>(x_op);
+      const float* yT = static_cast<const float*>(y_op);
+      st = half_step_ffma_launch(xT, ldx, xsq, xoff, yT, ldy, gc, log_b, nx, ny, d, eps, kappa, fh, workspace, ws_bytes,
+                                 s, dyn, 0);
+      if (st == TRNOPT_OK)
+        st = half_step_ffma_launch(yT, ldy, ysq, yoff, xT, ldx, fh, log_a, ny, nx, d, eps, kappa, gn, workspace,
+                                   ws_bytes, s, dyn, 1);
+    } else {
+      st = TRNOPT_ERR_INVALID_ARGUMENT;
+    }
+    if (st != TRNOPT_OK) return st;
+  }
+  return cuda_status(solve_check_launch(static_cast<TrnoptSolveState*>(state), n_iter, g0, g1, w_y, s));
 }
 
 int trnopt_max_change(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out, void* stream) {

@@ -201,7 +201,7 @@ int trnopt_sinkhorn_run_sharded(void* comm, const void* xpack, const float* xsq,
     pg.wait_epoch = c->epoch;
     pg.epoch = c->epoch + 1;
     st = half_step_tc_launch(yp, ysq + y0, yoff ? yoff + y0 : nullptr, xpack, fh, log_a, syr, nx, d, sy, sx, eps,
-                             kappa_y, gn + y0, workspace, ws_bytes, s, W > 1 ? &pg : nullptr);
+                             kappa_y, gn + y0, workspace, ws_bytes, s, W > 1 ? &pg : nullptr, nullptr, 1, true);
     if (st != TRNOPT_OK) return st;
     c->epoch = pg.epoch;
   }

@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/trnopt_cuda.h"
+
 namespace trnopt {
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -54,6 +56,8 @@ struct LseProblem {
   int mode;            // 0: write fh, 1: write lse (natural log)
   float* out;          // (rows,)
   int* error_word;     // device error flags
+  const TrnoptSolveState* dyn;   // nullptr, or the solve state whose stage gives eps and kappa (and done: return)
+  int side;            // with dyn: 0 = the f half-step (kappa[0]), 1 = the g half-step (kappa[1])
 };
 
 // Stream-K bookkeeping, computed on the host per launch.
@@ -101,7 +105,8 @@ __device__ __forceinline__ void lse_merge(float& M, float& l, float M2, float l2
 // way. The weights 2^(M_k - M) <= 1 come from ex2.approx (relative error ~2^-22, the level of the terms inside each
 // partial) and are summed with the partials in double precision, as is the rest of the epilogue. (Double-precision
 // exp2 here, inlined at every merge site, measured 4-7 % slower for the whole tensor-core kernel.)
-__device__ inline float finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride) {
+__device__ inline float finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride,
+                                   double eps, double kappa) {
   constexpr int kRegParts = 8;
   const float xsq = p.mode == 0 ? __ldg(p.xsq + row) : 0.f;
   const float off = (p.mode == 0 && p.off) ? __ldg(p.off + row) : 0.f;
@@ -124,7 +129,7 @@ __device__ inline float finish_row(const LseProblem& p, int row, const float2* p
   double lse = ((double)M + log2(l)) * kLn2;
   double res;
   if (p.mode == 0) {
-    res = p.kappa * ((double)xsq + p.eps * (double)off - p.eps * lse) - (double)xsq;
+    res = kappa * ((double)xsq + eps * (double)off - eps * lse) - (double)xsq;
   } else {
     res = lse;
   }

@@ -56,6 +56,15 @@ __device__ __forceinline__ void load_bias(float* dst, const LseProblem& p, int c
 }
 
 __global__ void __launch_bounds__(FF_THREADS, 2) lse_ffma_kernel(LseProblem p, StreamK sk) {
+  if (p.dyn != nullptr) {
+    // a run decided on the device: eps and kappa of the state's current stage; nothing to do once it is done
+    const TrnoptSolveState* st = p.dyn;
+    if (st->done) return;
+    p.dot2 = st->dot2;
+    p.gh2 = st->gh2;
+    p.eps = (double)st->eps;
+    p.kappa = (double)st->kappa[p.side];
+  }
   extern __shared__ __align__(16) float smem[];
   __shared__ int s_last;
   const int d = p.d;
@@ -174,7 +183,7 @@ __global__ void __launch_bounds__(FF_THREADS, 2) lse_ffma_kernel(LseProblem p, S
     if (s_last) {
       __threadfence();
       if (tid < FF_BM && r0 + tid < p.rows)
-        finish_row(p, r0 + tid, sk.partials + (size_t)r * sk.slots * FF_BM + tid, expected, FF_BM);
+        finish_row(p, r0 + tid, sk.partials + (size_t)r * sk.slots * FF_BM + tid, expected, FF_BM, p.eps, p.kappa);
       if (tid == 0) sk.counters[r] = 0;
     }
     u = seg_end;

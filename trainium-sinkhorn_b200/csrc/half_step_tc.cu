@@ -390,6 +390,8 @@ struct TcArgs {
   LseProblem p;
   StreamK sk;
   int dk;            // elements of each half (hi, lo) per packed row; multiple of 16
+  float dot2_scale;  // 2^-(sx + sy): p.dot2 is already scaled; a solve state's dot2 is scaled by this in the kernel
+  int mirror;        // 1 when the row cloud lies above the column cloud in memory: correction passes swapped
   Publish pub;       // world > 1: wait for the other GPUs' rows of gh, publish this GPU's rows of the output
 };
 
@@ -403,6 +405,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const LseProblem& p = args.p;
   const StreamK& sk = args.sk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The half-step's scalars: from the arguments, or (a run decided on the device) from the solve state's current
+  // stage, read before anything else; a state that is done leaves nothing to do. A launch that reads a state is
+  // ordered after the check that last wrote it (launched without programmatic overlap, or within a run in which
+  // no check runs).
+  float dot2_e = p.dot2, gh2_e = p.gh2;
+  double eps_e = p.eps, kappa_e = p.kappa;
+  if (p.dyn != nullptr) {
+    const TrnoptSolveState* st = p.dyn;
+    if (st->done) return;
+    dot2_e = st->dot2 * args.dot2_scale;
+    gh2_e = st->gh2;
+    eps_e = (double)st->eps;
+    kappa_e = (double)st->kappa[p.side];
+  }
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* full_b = bars;
@@ -518,7 +534,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // L2 round trip, overlapped with the MMAs of the tile before.
     const float* __restrict__ ghp = p.gh;
     const float* __restrict__ lbp = p.log_b;
-    const float inv_dot2 = 1.0f / p.dot2;
+    const float inv_dot2 = 1.0f / dot2_e;
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the previous grid (which may write gh) is complete
     int T = 0;
     bool ok = true;
@@ -545,7 +561,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint8_t* bb = smem + C::OFF_BIAS_B + bslot * kBiasBBytes;
 #pragma unroll
       for (int q = 0; q < TC_BN / 32; ++q) {
-        const float x = fmaf(l[q], p.lb2, g[q] * p.gh2) * inv_dot2;
+        const float x = fmaf(l[q], p.lb2, g[q] * gh2_e) * inv_dot2;
         *reinterpret_cast<uint2*>(bb + bias_row_offset(q * 32 + lane)) =
             bias_split(fminf(fmaxf(x, -1e36f), 1e36f) + (x == -INFINITY ? -INFINITY : 0.f));
       }
@@ -561,6 +577,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t b_base = smem_u32(smem + C::OFF_B);
       const uint32_t bias_a = smem_u32(smem + C::OFF_BIAS_A);
       const uint32_t bias_b = smem_u32(smem + C::OFF_BIAS_B);
+      const bool mirror = args.mirror != 0;
       for (long long u = u_begin; u < u_end && ok; ++seg) {
         const int r = (int)(u / sk.nct);
         const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
@@ -580,9 +597,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           uint32_t accumulate = 0;
 #pragma unroll
           for (int pass = 0; pass < 3; ++pass) {
-            // hi.lo and lo.hi first (the small corrections accumulate before the large hi.hi terms), then hi.hi
-            const int ea0 = (pass == 1) ? dk : 0;
-            const int eb0 = (pass == 0) ? dk : 0;
+            // The small correction products first, then hi.hi, in an order fixed by the two clouds rather than by
+            // their roles: P_hi.Q_lo, P_lo.Q_hi, P_hi.Q_hi with P the cloud at the lower address. The f half-step
+            // (x rows) and the g half-step (y rows) then accumulate x_i . y_j from the same products in the same
+            // order, identically rounded (the tensor cores round the accumulation toward zero). With the order tied
+            // to the roles the two half-steps see costs that differ in the last bits, and that difference drives the
+            // nearly free relative potential of mutually dominant point pairs a little further every iteration.
+            const int first = mirror ? 1 : 0;
+            const int ea0 = (pass == 1 - first) ? dk : 0;
+            const int eb0 = (pass == first) ? dk : 0;
             for (int kk = 0; kk < ksteps; ++kk) {
               const int ea = ea0 + 16 * kk, eb = eb0 + 16 * kk;
               const uint32_t sa = a_tile + (ea >> 6) * (TC_BM * 128) + (ea & 63) * 2;
@@ -617,7 +640,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int wg = warp >> 2;
     const int qrow = (warp & 3) * 32 + lane;   // this thread's row in the tile == its TMEM lane
     const uint32_t lane_base = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(wg * (TC_BN / 2));
-    const float dot2 = p.dot2;
+    const float dot2 = dot2_e;
     int T = 0;
     bool ok = true, published = false;
     for (long long u = u_begin; u < u_end;) {
@@ -651,7 +674,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __threadfence();
         const int row = r * TC_BM + qrow;
         if (row < p.rows) {
-          const float v = finish_row(p, row, base + qrow, expected, TC_BM);
+          const float v = finish_row(p, row, base + qrow, expected, TC_BM, eps_e, kappa_e);
           if (args.pub.world > 1) {
             publish_row(args.pub, row, v);
             published = true;
@@ -796,7 +819,8 @@ void tc_plan(int device, int rows, int m, int d, StreamK& sk) {
 size_t tc_partial_bytes(const StreamK& sk) { return (size_t)sk.nrt * sk.slots * TC_BM * sizeof(float2); }
 
 template <int NKB>
-static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, cudaStream_t stream) {
+static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, cudaStream_t stream,
+                               bool pdl) {
   using C = TcCfg<NKB>;
   static std::atomic<int> attr_done[kMaxDevices];
   cudaError_t e = smem_attr_once(reinterpret_cast<const void*>(half_step_tc_kernel<NKB>), C::SMEM, attr_done);
@@ -810,18 +834,20 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, half_step_tc_kernel<NKB>, ma, mb, a);
 }
 
 cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,
-                      cudaStream_t stream, const Publish* pub) {
+                      cudaStream_t stream, const Publish* pub, bool pdl) {
   const int kp = tc_kp(p.d);
   CUtensorMap ma, mb;
   if (!tensor_map(xpack, p.rows, kp, TC_BM, &ma) || !tensor_map(ypack, p.m, kp, TC_BN, &mb))
     return cudaErrorInvalidValue;
   TcArgs a;
   a.p = p;
+  a.dot2_scale = (float)ldexp(1.0, -(sx + sy));
+  a.mirror = reinterpret_cast<uintptr_t>(xpack) > reinterpret_cast<uintptr_t>(ypack);
   a.p.dot2 = (float)((double)p.dot2 * ldexp(1.0, -(sx + sy)));
   a.sk = sk;
   a.dk = tc_dk(p.d);
@@ -831,8 +857,8 @@ cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack,
     a.pub = Publish{};
     a.pub.world = 1;
   }
-  if (kp == 64) return tc_launch_t<1>(ma, mb, a, stream);
-  return tc_launch_t<2>(ma, mb, a, stream);
+  if (kp == 64) return tc_launch_t<1>(ma, mb, a, stream, pdl);
+  return tc_launch_t<2>(ma, mb, a, stream, pdl);
 }
 
 }  // namespace trnopt

@@ -42,11 +42,13 @@ void tc_plan(int device, int rows, int m, int d, StreamK& sk);
 size_t tc_partial_bytes(const StreamK& sk);
 cudaError_t tc_pack(const float* xT, int ldx, int n, int d, int scale_exp, void* packed, cudaStream_t stream);
 cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,
-                      cudaStream_t stream, const Publish* pub = nullptr);
+                      cudaStream_t stream, const Publish* pub = nullptr, bool pdl = true);
 
 // companions (companions.cu)
 cudaError_t balanced_error_launch(const float* gh_old, const float* gh_new, const float* w, int n, float inv_eps,
                                   float* out, cudaStream_t stream);
+cudaError_t recenter_launch(float* gh, int n, int npad, double* gauge, const TrnoptSolveState* st,
+                            cudaStream_t stream);
 cudaError_t max_change_launch(const float* gh_old, const float* gh_new, int n, float inv_eps, float* out,
                               cudaStream_t stream);
 
@@ -77,6 +79,28 @@ int half_step_tc_check(const void* xpack, const float* xsq, const void* ypack, c
 // The tcgen05 half-step behind trnopt_half_step_tc, with an optional Publish (capi.cu); returns a TRNOPT status.
 int half_step_tc_launch(const void* xpack, const float* xsq, const float* off, const void* ypack, const float* gh,
                         const float* log_b, int rows, int m, int d, int sx, int sy, float eps, float kappa, float* fh,
-                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub);
+                        void* workspace, size_t ws_bytes, cudaStream_t stream, const Publish* pub,
+                        const TrnoptSolveState* dyn = nullptr, int side = 0, bool pdl = true);
+
+// The FFMA half-step behind trnopt_half_step, optionally reading its scalars from a solve state (capi.cu).
+int half_step_ffma_launch(const float* xT, int ldx, const float* xsq, const float* off, const float* yT, int ldy,
+                          const float* gh, const float* log_b, int rows, int m, int d, float eps, float kappa, float* fh,
+                          void* workspace, size_t ws_bytes, cudaStream_t stream, const TrnoptSolveState* dyn,
+                          int side);
+
+// The solver loop's check after a run of n iterations (companions.cu): advances the state's counters and applies
+// the reference loop's stage and convergence rules.
+cudaError_t solve_check_launch(TrnoptSolveState* st, int n, const float* g0, const float* g1, const float* w,
+                               cudaStream_t stream);
+// A stage's half-step parameters, computed as a host call computes them (float eps, float kappa, float dot2 / gh2).
+__host__ __device__ inline void solve_stage_params(TrnoptSolveState& st) {
+  const int s = st.stage < st.n_stages ? st.stage : st.n_stages;
+  const double e = st.stage_eps[s];
+  st.eps = (float)e;
+  const double inv = 1.0 / (double)st.eps;
+  st.dot2 = (float)(2.0 * inv * 1.4426950408889634);
+  st.gh2 = (float)(inv * 1.4426950408889634);
+  for (int k = 0; k < 2; ++k) st.kappa[k] = st.rho[k] < 0.0 ? 1.0f : (float)(st.rho[k] / (st.rho[k] + e));
+}
 
 }  // namespace trnopt

@@ -196,9 +196,10 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prepare_cloud_kernel(const Pr
 }
 
 __global__ void unshift_kernel(const float* __restrict__ h, const double* __restrict__ sq, int n,
-                               double* __restrict__ out) {
+                               const double* __restrict__ gauge, double sign, double* __restrict__ out) {
+  const double c = gauge ? sign * gauge[0] : 0.0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
-    out[i] = (double)h[i] + sq[i];
+    out[i] = ((double)h[i] + sq[i]) + c;
 }
 
 __global__ void take_error_kernel(int* word, double* out) { out[0] = (double)atomicExch(word, 0); }
@@ -274,11 +275,12 @@ int trnopt_prepare_cloud(const double* pts, int n, int d, int npad, const double
   return cudaGetLastError() == cudaSuccess ? TRNOPT_OK : TRNOPT_ERR_CUDA;
 }
 
-int trnopt_unshift(const float* h, const double* sq, int n, double* out, void* stream) {
-  if (!h || !sq || !out || n < 1) return TRNOPT_ERR_INVALID_ARGUMENT;
-  if (!aligned8(sq) || !aligned8(out)) return TRNOPT_ERR_ALIGNMENT;
+int trnopt_unshift(const float* h, const double* sq, int n, const double* gauge, int sign, double* out,
+                   void* stream) {
+  if (!h || !sq || !out || n < 1 || (sign != 1 && sign != -1)) return TRNOPT_ERR_INVALID_ARGUMENT;
+  if (!aligned8(sq) || !aligned8(out) || (gauge && !aligned8(gauge))) return TRNOPT_ERR_ALIGNMENT;
   const int blocks = (n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184;
-  unshift_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(h, sq, n, out);
+  unshift_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(h, sq, n, gauge, (double)sign, out);
   return cudaGetLastError() == cudaSuccess ? TRNOPT_OK : TRNOPT_ERR_CUDA;
 }
 

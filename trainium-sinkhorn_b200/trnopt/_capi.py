@@ -67,7 +67,11 @@ _SIGS = {
     "trnopt_cloud_stats_scratch_bytes": (_Z, [_I]),
     "trnopt_cloud_stats": (_I, [_P, _I, _P, _I, _I, _P, _P, _Z, _P]),
     "trnopt_prepare_cloud": (_I, [_P, _I, _I, _I, _P, _D, _P, _I, _P, _D, _P, _P, _P, _P, _P, _P, _P]),
-    "trnopt_unshift": (_I, [_P, _P, _I, _P, _P]),
+    "trnopt_unshift": (_I, [_P, _P, _I, _P, _I, _P, _P]),
+    "trnopt_recenter": (_I, [_P, _I, _I, _P, _P, _P]),
+    "trnopt_solve_init": (_I, [_P, _P, _I, _D, _D, _D, _I, _I, _I, _I, _I, _F, _F, _I, _I, _I, _P]),
+    "trnopt_sinkhorn_run_checked": (_I, [_I, _P, _I, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P, _P,
+                                         _I, _I, _P, _P, _P, _Z, _P]),
     "trnopt_take_error_flags": (_I, [_P, _P]),
     "trnopt_plan_rows": (_I, [_P, _I, _P, _I, _I, _P, _P, _P, _P, _D, _P, _I, _P, _P]),
     "trnopt_plan_workspace_size": (_Z, [_I, _I]),
@@ -303,9 +307,50 @@ def prepare_cloud(pts: torch.Tensor, n: int, npad: int, center, r: float, shift,
                                    _ptr(xT), _ptr(vec), _ptr(sq64), _ptr(gh0), _stream()), "trnopt_prepare_cloud")
 
 
-def unshift(h, sq, n: int, out) -> None:
-    """out[:n] = h[:n] + sq[:n] in float64 (device tensors; out may be a view into a larger buffer)."""
-    check(lib.trnopt_unshift(_ptr(h), _ptr(sq), n, _ptr(out), _stream()), "trnopt_unshift")
+def unshift(h, sq, n: int, out, gauge=None, sign: int = 1) -> None:
+    """out[:n] = h[:n] + sq[:n] + sign * gauge[0] in float64 (device tensors; out may be a view into a larger
+    buffer; gauge None = 0)."""
+    check(lib.trnopt_unshift(_ptr(h), _ptr(sq), n, _ptr(gauge), int(sign), _ptr(out), _stream()), "trnopt_unshift")
+
+
+def recenter(gh, n: int, npad: int, gauge, state=None) -> None:
+    """Balanced solves: gh -= K (its float32-rounded mean over the first n entries), gauge[0] += K; nothing once a
+    solve state (if given) is done."""
+    check(lib.trnopt_recenter(_ptr(gh), n, npad, _ptr(gauge), _ptr(state), _stream()), "trnopt_recenter")
+
+
+MAX_STAGES = 32
+
+
+class SolveState(ctypes.Structure):
+    """Host mirror of TrnoptSolveState (include/trnopt_cuda.h), to read a copy of the device state."""
+    _fields_ = [("stage_eps", _D * (MAX_STAGES + 1)), ("rho", _D * 2), ("tol", _F), ("stage_tol", _F),
+                ("n_stages", _I), ("check_every", _I), ("max_iters", _I), ("stage_max_iters", _I),
+                ("fixed_iters", _I), ("balanced", _I), ("sched_len", _I), ("n_real", _I), ("npad", _I),
+                ("eps", _F), ("kappa", _F * 2), ("dot2", _F), ("gh2", _F),
+                ("it", _I), ("stage", _I), ("stage_it", _I), ("done", _I), ("converged", _I), ("err", _F),
+                ("stage_iters", _I * (MAX_STAGES + 1))]
+
+
+def solve_init(state, stages, final_eps, rho_x, rho_y, check_every, max_iters, stage_max_iters, fixed_iters,
+               sched_len, tol, stage_tol, n_real, npad, it0) -> None:
+    """Write the plan and starting counters into a device TrnoptSolveState (state: a CUDA uint8 tensor)."""
+    import numpy as np
+    st = np.ascontiguousarray(stages if len(stages) else [0.0], dtype=np.float64)
+    check(lib.trnopt_solve_init(_ptr(state), st.ctypes.data_as(_P), len(stages), float(final_eps),
+                                float(-1.0 if rho_x is None else rho_x), float(-1.0 if rho_y is None else rho_y),
+                                int(check_every), int(max_iters), int(stage_max_iters), int(bool(fixed_iters)),
+                                int(sched_len), float(tol), float(stage_tol), int(n_real), int(npad), int(it0),
+                                _stream()), "trnopt_solve_init")
+
+
+def sinkhorn_run_checked(path, x_op, ldx, xsq, xoff, log_a, nx, sx, y_op, ldy, ysq, yoff, log_b, ny, sy, d, g0, g1,
+                         fh, start_parity, n_iter, state, w_y, ws) -> None:
+    """Queue n_iter iterations at the solve state's current eps stage, then the check at their end."""
+    check(lib.trnopt_sinkhorn_run_checked(path, _ptr(x_op), ldx, _ptr(xsq), _ptr(xoff), _ptr(log_a), nx, int(sx),
+                                          _ptr(y_op), ldy, _ptr(ysq), _ptr(yoff), _ptr(log_b), ny, int(sy), d,
+                                          _ptr(g0), _ptr(g1), _ptr(fh), int(start_parity), int(n_iter), _ptr(state),
+                                          _ptr(w_y), _ptr(ws), ws.numel(), _stream()), "trnopt_sinkhorn_run_checked")
 
 
 def take_error_flags(out) -> None:

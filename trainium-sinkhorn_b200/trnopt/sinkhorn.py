@@ -25,6 +25,7 @@ path), or by an NCCL all-gather after each half-step ("nccl").
 
 from __future__ import annotations
 
+import ctypes
 import time
 from dataclasses import dataclass, field
 
@@ -291,6 +292,15 @@ class _Buffers:
         self.out = torch.empty(2 * (n + m) + 1, dtype=torch.float64, device=dev)
         self.out_host = torch.empty(2 * (n + m) + 1, dtype=torch.float64, pin_memory=True)
         self.err = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.gauge = torch.zeros(1, dtype=torch.float64, device=dev)     # balanced: offset taken out of g
+        self.state = torch.zeros(ctypes.sizeof(_capi.SolveState), dtype=torch.uint8, device=dev)
+        self.state_host = torch.zeros(ctypes.sizeof(_capi.SolveState), dtype=torch.uint8, pin_memory=True)
+
+    def read_state(self) -> "_capi.SolveState":
+        """The device solve state, copied to the host (synchronises the stream)."""
+        self.state_host.copy_(self.state, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return _capi.SolveState.from_buffer_copy(self.state_host.numpy().tobytes())
 
     def frame(self, center: np.ndarray, r: float) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
         """After the statistics are on the host: the internal frame's translation (the joint mean of the
@@ -404,6 +414,55 @@ def _workspace(X: _Cloud, Y: _Cloud, shards: int, dev: torch.device, path: str =
     return _capi.new_workspace(need, dev)
 
 
+def _device_loop(B, runner, path, opts, stages, sched, balanced, rho_x, rho_y, tol, stage_tol, kap):
+    """The loop of sinkhorn.py:346-378 on one GPU with its decisions taken on the device. The eps-scaling prefix
+    (eps changes every iteration, no checks) is queued from the host; from there on every run of iterations ends in
+    a check kernel that applies the reference loop's rules to a solve state in device memory (trnopt_solve_init /
+    trnopt_sinkhorn_run_checked): stage moves, convergence, max_iters. Runs are queued a chunk at a time and the state
+    is read once per chunk; runs queued past convergence return at once. The chunk grows from 2 runs with the
+    number of runs the last two checks' error ratio predicts are left (at most 16; all of them for fixed_iters).
+    Returns (iterations, error, converged, stage iterations)."""
+    X, Y, G, fh, ws = runner.X, runner.Y, runner.G, runner.fh, runner.step.ws
+    tc = path == "tc"
+    it = 0
+    for i in range(min(len(sched), opts.max_iters)):
+        if balanced:
+            _capi.recenter(G[i % 2], Y.n, Y.npad, B.gauge)
+        runner.run(i, 1, sched[i], kap(sched[i], rho_x), kap(sched[i], rho_y))
+        it = i + 1
+    _capi.solve_init(B.state, stages, opts.eps, rho_x, rho_y, opts.check_every, opts.max_iters,
+                     opts.stage_max_iters, opts.fixed_iters, len(sched), tol, stage_tol, Y.n, Y.npad, it)
+    runs = []
+    while it < opts.max_iters:
+        n = min(opts.check_every - it % opts.check_every, opts.max_iters - it)
+        runs.append((it, n))
+        it += n
+    chunk, k, prev = (len(runs) if opts.fixed_iters else 2), 0, None
+    while k < len(runs):
+        for it0, n in runs[k:k + chunk]:
+            if balanced:
+                _capi.recenter(G[it0 % 2], Y.n, Y.npad, B.gauge, B.state)
+            _capi.sinkhorn_run_checked(_capi.PATH_TC if tc else _capi.PATH_FFMA, X.packed if tc else X.xT, X.npad,
+                                       X.sq, X.off, X.log_w, X.npad, X.sexp, Y.packed if tc else Y.xT, Y.npad, Y.sq,
+                                       Y.off, Y.log_w, Y.npad, Y.sexp, X.d, G[0], G[1], fh, it0 % 2, n, B.state,
+                                       Y.w, ws)
+        k += chunk
+        st = B.read_state()
+        if st.done:
+            break
+        chunk = 16
+        e = float(st.err)
+        if prev is not None and np.isfinite(e) and 0.0 < e < prev[0] and prev[0] > 0.0:
+            rate = (e / prev[0]) ** (1.0 / max(1, k - prev[1]))
+            if 0.0 < rate < 1.0 and e > tol:
+                chunk = int(min(16, max(1, np.ceil(np.log(tol / e) / np.log(rate)))))
+        if np.isfinite(e):
+            prev = (e, k)
+    st = B.read_state()
+    stage_iters = list(st.stage_iters[:st.stage]) + ([st.stage_it] if stages else [])
+    return int(st.it), float(st.err), bool(st.converged), stage_iters
+
+
 def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target=None,
              b_target=None) -> SinkhornResult:
     """Entropic OT between point clouds x (n, d) and y (m, d) with weights a, b (default uniform): the reference's
@@ -493,6 +552,7 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         X.prepare(center, r, shift, log_a[0])
         Y.prepare(center, r, shift, log_b[0], gh0=G[0])
         fh.zero_()
+        B.gauge.zero_()
         if peer is not None:
             peer.arrive()                                  # the others may write into these buffers from here on
         err_dev = B.err
@@ -502,7 +562,10 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
         stage_tol = max(opts.stage_tol, 1e-5)              # float32 floors (sinkhorn.py:342-344)
         tol = max(opts.tol, 5e-6) if not balanced else opts.tol
         t0 = time.perf_counter()
-        while it < opts.max_iters:
+        if shards == 1:
+            it, err, converged, stage_iters = _device_loop(B, runner, path, opts, stages, sched, balanced, rho_x,
+                                                           rho_y, tol, stage_tol, kap)
+        while shards > 1 and it < opts.max_iters:
             # The loop of sinkhorn.py:346-378, advanced a run of iterations at a time: a run ends where the host
             # has to look (a check, an eps change, max_iters), so the iterations inside it are one C call.
             if stages:
@@ -514,6 +577,9 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
             else:
                 n = opts.check_every - (stage_it % opts.check_every)
             n = min(n, opts.max_iters - it)
+            if balanced:
+                # the run's input potential moved to mean zero, the offset kept in float64 (trnopt_recenter)
+                _capi.recenter(G[it % 2], Y.n, Y.npad, B.gauge)
             runner.run(it, n, e, kap(e, rho_x), kap(e, rho_y))
             runner.sync()
             it += n
@@ -539,15 +605,16 @@ def sinkhorn(x, y, a=None, b=None, opts: SinkhornOptions | None = None, a_target
             if check and err < tol:
                 converged = True
                 break
-        if stages:
+        if stages and shards > 1:
             stage_iters.append(stage_it)
         gh = G[it % 2]
         # Unshift on the device into one float64 buffer (f, g, and for unbalanced the balanced half-steps' fb, gb),
         # the error flags at its end, one download (sinkhorn.py:375-389).
         nx, ny = X.n, Y.n
         out = B.out
-        _capi.unshift(fh, X.sq64, nx, out)
-        _capi.unshift(gh, Y.sq64, ny, _Off(out, nx, 8))
+        gauge = B.gauge if balanced else None
+        _capi.unshift(fh, X.sq64, nx, out, gauge, -1)
+        _capi.unshift(gh, Y.sq64, ny, _Off(out, nx, 8), gauge, 1)
         if not balanced:
             # The plan's marginals from one balanced (kappa = 1, no offset) update each way (sinkhorn.py:381-389).
             hx = step(X, Y, gh, opts.eps, 1.0, use_off=False, out=B.hb[:X.npad])
