@@ -265,12 +265,14 @@ __device__ __forceinline__ bool block_fold(const float (&a)[N], float cmax, floa
   return false;
 }
 
-// First block of a row (M still at the floor): max first, then M = max + kLazyHeadroom.
-template <int N>
-__device__ __forceinline__ void block_first(const float (&a)[N], float cmax, float& M, float& L) {
-  if (!(cmax > kMaxFloor)) return;                            // only columns past m so far
-  M = cmax + kLazyHeadroom;
-  L = exp_sum(a, M);
+// M for a row's first block (M still at the floor): the block's largest raw value * dot2 + kLazyHeadroom, so the
+// block's terms are then formed against it with one rounding like every other block's; the floor again for a block
+// of columns past m only (all -inf).
+__device__ __forceinline__ float block_start_ref(const uint32_t (&v)[64], float dot2) {
+  float c[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int q = 0; q < 32; ++q) c[q & 3] = fmax3(c[q & 3], __uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
+  return fmaxf(fmaf(fmaxf(fmaxf(c[0], c[1]), fmaxf(c[2], c[3])), dot2, kLazyHeadroom), kMaxFloor);
 }
 
 // Fold one row's 128 accumulator values of a tile (TMEM address taddr, 32x32b lanes: this thread's row) into the
@@ -290,12 +292,10 @@ __device__ __forceinline__ void lse_tile128(uint32_t taddr, float dot2, float& M
 #pragma unroll
   for (int j = 0; j < N; ++j) asm volatile("" : "+r"(v[j]));
   // block 0
-  bool first = (M == kMaxFloor);
-  block_terms(v, d2, first ? 0.f : M, a, cmax);
+  if (M == kMaxFloor) M = block_start_ref(v, dot2);
+  block_terms(v, d2, M, a, cmax);
   TRNOPT_TMEM_LD64(taddr + (uint32_t)N, v);                   // block 1 into the now-free registers
-  bool redo = false;
-  if (first) block_first(a, cmax, M, L);
-  else redo = block_fold(a, cmax, M, L);
+  bool redo = block_fold(a, cmax, M, L);
   tmem_wait_ld();
 #pragma unroll
   for (int j = 0; j < N; ++j) asm volatile("" : "+r"(v[j]));
@@ -305,14 +305,13 @@ __device__ __forceinline__ void lse_tile128(uint32_t taddr, float dot2, float& M
     L = r.y;
   }
   // block 1: terms and max, then its redo re-read if any, then release the accumulator, then the exps
-  first = (M == kMaxFloor);
-  block_terms(v, d2, first ? 0.f : M, a, cmax);
-  redo = !first && cmax > kLazyRedo;
+  if (M == kMaxFloor) M = block_start_ref(v, dot2);
+  block_terms(v, d2, M, a, cmax);
+  redo = cmax > kLazyRedo;
   if (__any_sync(0xffffffffu, redo)) {
     // Rare: lanes without a redo fold block 1 first (a[] is then free), then the warp re-reads it for the others,
     // then releases.
-    if (first) block_first(a, cmax, M, L);
-    else if (!redo) block_fold(a, cmax, M, L);
+    if (!redo) block_fold(a, cmax, M, L);
     const float2 r = block_redo(taddr + (uint32_t)N, dot2, redo, M, L);
     M = r.x;
     L = r.y;
@@ -321,8 +320,7 @@ __device__ __forceinline__ void lse_tile128(uint32_t taddr, float dot2, float& M
   } else {
     tmem_fence_before();
     mbar_arrive(acc_empty);
-    if (first) block_first(a, cmax, M, L);
-    else block_fold(a, cmax, M, L);
+    block_fold(a, cmax, M, L);
   }
 }
 
@@ -433,6 +431,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   int* s_last = reinterpret_cast<int*>(smem + C::OFF_MISC + 16);     // [2], one per epilogue warpgroup
+  int* s_pend = reinterpret_cast<int*>(smem + C::OFF_MISC + 24);     // [2][2]: pending row tile, its arrivals
 
   if (blockDim.x != TC_THREADS) {
     if (threadIdx.x == 0) atomicOr(p.error_word, (int)kErrBadLaunch);
@@ -643,17 +642,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const float dot2 = dot2_e;
     int T = 0;
     bool ok = true, published = false;
+    // A segment's arrival on its row tile's counter is an acquire-release atomic by one thread after the warpgroup's
+    // partial stores and a warpgroup barrier (the release covers the barrier's other threads' stores); its result
+    // -- whether this warpgroup is the row tile's last arrival and merges it -- is looked at one tile later (or at
+    // the end of the range), so the atomic's round trip to L2 overlaps the next tile's fold instead of stalling it.
+    bool pending = false;
+    int pend_old = 0;   // the atomic's result (thread qrow 0)
+#define TRNOPT_RESOLVE_ARRIVAL()                                                                        \
+  do {                                                                                                  \
+    if (qrow == 0) s_last[wg] = (pend_old == s_pend[2 * wg + 1] - 1);                                   \
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");                                         \
+    if (s_last[wg]) {                                                                                   \
+      const int pend_r = s_pend[2 * wg], pend_expected = s_pend[2 * wg + 1];                             \
+      const int row = pend_r * TC_BM + qrow;                                                            \
+      if (row < p.rows) {                                                                               \
+        const float2* base = sk.partials + (size_t)pend_r * sk.slots * TC_BM;                           \
+        const float v = finish_row(p, row, base + qrow, pend_expected, TC_BM, eps_e, kappa_e);          \
+        if (args.pub.world > 1) {                                                                       \
+          publish_row(args.pub, row, v);                                                                \
+          published = true;                                                                             \
+        }                                                                                               \
+      }                                                                                                 \
+      if (qrow == 0) sk.counters[pend_r] = 0;                                                           \
+    }                                                                                                   \
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory"); /* s_last read before its next write */ \
+    pending = false;                                                                                    \
+  } while (0)
     for (long long u = u_begin; u < u_end;) {
       const int r = (int)(u / sk.nct);
       const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
       float M = kMaxFloor, L = 0.f;
       for (; u < seg_end; ++u, ++T) {
-        if (!ok) continue;
-        const int acc = T % TC_NACC;
-        ok = mbar_wait(&acc_full[acc], (T / TC_NACC) & 1, abort_flag, p.error_word);
-        if (!ok) continue;
-        tmem_fence_after();
-        lse_tile128(lane_base + (uint32_t)(acc * TC_BN), dot2, M, L, &acc_empty[acc]);
+        if (ok) {
+          const int acc = T % TC_NACC;
+          ok = mbar_wait(&acc_full[acc], (T / TC_NACC) & 1, abort_flag, p.error_word);
+          if (ok) {
+            tmem_fence_after();
+            lse_tile128(lane_base + (uint32_t)(acc * TC_BN), dot2, M, L, &acc_empty[acc]);
+          }
+        }
+        if (pending) TRNOPT_RESOLVE_ARRIVAL();
       }
       // Segment done: this warpgroup's partial for row tile r, then one arrival on the row tile's counter.
       const long long first_u = (long long)r * sk.nct;
@@ -661,28 +689,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int klast = sk_cta_of(first_u + sk.nct - 1, sk.units, sk.grid);
       const int expected = 2 * (klast - kfirst + 1);
       const int slot = 2 * (blockIdx.x - kfirst) + wg;
-      float2* base = sk.partials + (size_t)r * sk.slots * TC_BM;
-      base[(size_t)slot * TC_BM + qrow] = make_float2(M, L);
-      __threadfence();
+      sk.partials[((size_t)r * sk.slots + slot) * TC_BM + qrow] = make_float2(M, L);
       asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
       if (qrow == 0) {
-        const int old = atomicAdd(&sk.counters[r], 1);
-        s_last[wg] = (old == expected - 1);
+        s_pend[2 * wg] = r;
+        s_pend[2 * wg + 1] = expected;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(pend_old) : "l"(sk.counters + r) : "memory");
       }
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
-      if (s_last[wg]) {
-        __threadfence();
-        const int row = r * TC_BM + qrow;
-        if (row < p.rows) {
-          const float v = finish_row(p, row, base + qrow, expected, TC_BM, eps_e, kappa_e);
-          if (args.pub.world > 1) {
-            publish_row(args.pub, row, v);
-            published = true;
-          }
-        }
-        if (qrow == 0) sk.counters[r] = 0;
-      }
+      pending = true;
     }
+    if (pending) TRNOPT_RESOLVE_ARRIVAL();
+#undef TRNOPT_RESOLVE_ARRIVAL
     if (published) __threadfence_system();   // this thread's peer stores, before the CTA barrier below
   }
 
