@@ -40,6 +40,7 @@ constexpr int TC_BN = 256;          // columns per tile (MMA N)
 constexpr int TC_NACC = 2;          // TMEM accumulators of TC_BN columns (512 columns in all)
 constexpr int TC_THREADS = 352;     // 8 epilogue warps + TMA producer + MMA + bias
 constexpr int TC_NBB = 2;           // column-bias operand slots (one per tile in flight between bias warp and MMA)
+constexpr int kTcPolyExps = 8;     // of every 64 exps of the fold, how many run on the FMA pipe
 constexpr int TC_PRODUCER_WARP = 8;
 constexpr int TC_MMA_WARP = 9;
 constexpr int TC_BIAS_WARP = 10;
@@ -202,17 +203,28 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __uint_as_float(__float_as_uint(p) + (__float_as_uint(y) << 23));
 }
 
-// sum_j 2^(a_j - off) on MUFU (ex2.approx), four independent packed partial sums.
-template <int N>
+// 2^x of a pair: on the FMA pipe (ex2_poly) when `poly`, else on MUFU (ex2.approx). (`poly` is a constant once
+// the callers' loops are unrolled.)
+__device__ __forceinline__ uint64_t ex2_pair(bool poly, float x, float y) {
+  return poly ? pk2(ex2_poly(x), ex2_poly(y)) : pk2(ex2_approx(x), ex2_approx(y));
+}
+
+// sum_j 2^(a_j - off), four independent packed partial sums. kPoly of every 64 values (spread evenly over the value
+// pairs) take the FMA-pipe polynomial, the rest MUFU: MUFU does 16 exps per clock per SM, and the fold has issue
+// slots and FMA-pipe cycles to spare beside it.
+template <int N, int kPoly = 0>
 __device__ __forceinline__ float exp_sum(const float (&a)[N], float off) {
   uint64_t s0 = 0ull, s1 = 0ull, s2 = 0ull, s3 = 0ull;
+  constexpr int kPolyPairs = kPoly / 2;
+#define TRNOPT_POLY_PAIR(pair) (kPolyPairs > 0 && ((pair) * kPolyPairs) % (N / 2) < kPolyPairs)
 #pragma unroll
   for (int j = 0; j < N; j += 8) {
-    s0 = fadd2(s0, pk2(ex2_approx(a[j] - off), ex2_approx(a[j + 1] - off)));
-    s1 = fadd2(s1, pk2(ex2_approx(a[j + 2] - off), ex2_approx(a[j + 3] - off)));
-    s2 = fadd2(s2, pk2(ex2_approx(a[j + 4] - off), ex2_approx(a[j + 5] - off)));
-    s3 = fadd2(s3, pk2(ex2_approx(a[j + 6] - off), ex2_approx(a[j + 7] - off)));
+    s0 = fadd2(s0, ex2_pair(TRNOPT_POLY_PAIR(j / 2), a[j] - off, a[j + 1] - off));
+    s1 = fadd2(s1, ex2_pair(TRNOPT_POLY_PAIR(j / 2 + 1), a[j + 2] - off, a[j + 3] - off));
+    s2 = fadd2(s2, ex2_pair(TRNOPT_POLY_PAIR(j / 2 + 2), a[j + 4] - off, a[j + 5] - off));
+    s3 = fadd2(s3, ex2_pair(TRNOPT_POLY_PAIR(j / 2 + 3), a[j + 6] - off, a[j + 7] - off));
   }
+#undef TRNOPT_POLY_PAIR
   s0 = fadd2(s0, s1);
   s2 = fadd2(s2, s3);
   s0 = fadd2(s0, s2);
@@ -252,7 +264,7 @@ static __device__ __noinline__ float2 block_redo(uint32_t taddr, float dot2, boo
 // (max <= M + kLazyRedo); returns true when the block must be redone in absolute terms instead.
 template <int N>
 __device__ __forceinline__ bool block_fold(const float (&a)[N], float cmax, float& M, float& L) {
-  const float sum = exp_sum(a, 0.f);
+  const float sum = exp_sum<N, kTcPolyExps>(a, 0.f);
   if (cmax <= kLazyMax) {
     L += sum;
   } else if (cmax <= kLazyRedo) {
