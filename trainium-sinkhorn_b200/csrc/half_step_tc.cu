@@ -687,7 +687,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (; u < seg_end; ++u, ++T) {
         if (ok) {
           const int acc = T % TC_NACC;
-          ok = mbar_wait(&acc_full[acc], (T / TC_NACC) & 1, abort_flag, p.error_word);
+          // (one decision per warp: the tile's TMEM loads are warp-collective)
+          ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (T / TC_NACC) & 1, abort_flag, p.error_word));
           if (ok) {
             tmem_fence_after();
             lse_tile128(lane_base + (uint32_t)(acc * TC_BN), dot2, M, L, &acc_empty[acc]);
