@@ -196,9 +196,20 @@ def wot_small():
     tm = wot_transport_map(x0, x1, growth, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=1e-8,
                            opts=opts)
     r = tm.result
-    np.savez_compressed(HERE / "wot_small.npz", f=r.f, g=r.g, row_mass=r.row_mass, col_mass=r.col_mass,
-                        iterations=tm.iterations, last_iterations=r.iterations, cost_scale=r.cost_scale,
-                        center=r.center, learned=np.stack(tm.learned_growth))
+    out = dict(f=r.f, g=r.g, row_mass=r.row_mass, col_mass=r.col_mass, iterations=tm.iterations,
+               last_iterations=r.iterations, cost_scale=r.cost_scale, center=r.center,
+               learned=np.stack(tm.learned_growth))
+    # the same map under the float32 stopping rule (tol 1e-8 -> 5e-6, stage tol -> 1e-5: sinkhorn.py:342-344) in
+    # float64 ("f64c") and the reference's own float32 run, as for the full-size config 3
+    for tag, dt, tol, stol in (("f64c", torch.float64, 5e-6, 1e-5), ("f32", torch.float32, 1e-8, 1e-6)):
+        tm = wot_transport_map(x0, x1, growth, eps=0.05, lambda1=1.0, lambda2=50.0, growth_iters=3, tol=tol,
+                               stage_tol=stol, opts=ref_sk.SinkhornOptions(backend=_recording(dt)))
+        r = tm.result
+        st = np.float32 if tag == "f32" else np.float64
+        out[f"{tag}_f"], out[f"{tag}_g"] = r.f.astype(st), r.g.astype(st)
+        out[f"{tag}_row_mass"], out[f"{tag}_col_mass"] = r.row_mass, r.col_mass
+        out[f"{tag}_meta"] = np.array([tm.iterations, r.iterations, r.error, r.cost_scale])
+    np.savez_compressed(HERE / "wot_small.npz", **out)
 
 
 def _example(name):
