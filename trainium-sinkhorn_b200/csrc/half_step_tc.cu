@@ -161,8 +161,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// One block of 64 values of a row relative to `shift` (0 for a row's first block): u_j = acc_j * dot2 - shift (the
-// column bias is already in the accumulator), their max, and the values themselves in a[].
+// One block of 64 values of a row relative to `shift` (the row's running max M): u_j = acc_j * dot2 - shift, one
+// packed FMA per two values (the column bias is already in the accumulator), their max, and the values in a[].
 template <int N>
 __device__ __forceinline__ void block_terms(uint32_t (&v)[N], uint64_t d2, float shift, float (&a)[N], float& cmax) {
   const uint64_t nm = pk2(-shift, -shift);
@@ -258,7 +258,7 @@ static __device__ __noinline__ float2 block_redo(uint32_t taddr, float dot2, boo
   return make_float2(Mn, L * ex2_approx(M - Mn) + exp_sum(a, Mn));
 }
 
-// Lazy-max update of (M, L) with a block whose values a[] are relative to M (not a first block): the exps use the
+// Lazy-max update of (M, L) with a block whose values a[] are relative to M: the exps use the
 // max known before the block, so no exp waits for the block's max (reduced alongside). Terms may exceed 1 by up
 // to 2^kLazyMax; a block whose max is higher rescales its sum (no new exps) while no term can have overflowed
 // (max <= M + kLazyRedo); returns true when the block must be redone in absolute terms instead.
@@ -289,10 +289,11 @@ __device__ __forceinline__ float block_start_ref(const uint32_t (&v)[64], float 
 
 // Fold one row's 128 accumulator values of a tile (TMEM address taddr, 32x32b lanes: this thread's row) into the
 // row's running base-2 (M, L):   t_j = acc_j * dot2 (the accumulator holds x.y plus the column bias / dot2),
-// L = sum_j 2^(t_j - M). Two blocks of 64 values (u_j = t_j - M from one packed FMA, acc * dot2 - M). Block 1 is loaded from TMEM
-// while block 0's exps run; once block 1 is loaded and its max (and any redo re-read) is done, every TMEM read of
-// the tile is over and the accumulator is released (tcgen05 fence, then an arrival on `acc_empty`) before block 1's
-// exps, so the MMAs two tiles ahead overlap them. Must be called by all 32 lanes of the warp.
+// L = sum_j 2^(t_j - M). Two blocks of 64 values (u_j = t_j - M from one packed FMA, acc * dot2 - M); a block that
+// finds M at the floor (the segment's first) sets M from its own max first. Block 1 is loaded from TMEM while block
+// 0's exps run; once block 1 is loaded and its max (and any redo re-read) is done, every TMEM read of the tile is over
+// and the accumulator is released (tcgen05 fence, then an arrival on `acc_empty`) before block 1's exps, so the MMAs
+// two tiles ahead overlap them. Must be called by all 32 lanes of the warp.
 __device__ __forceinline__ void lse_tile128(uint32_t taddr, float dot2, float& M, float& L, uint64_t* acc_empty) {
   constexpr int N = 64;
   const uint64_t d2 = pk2(dot2, dot2);
