@@ -314,7 +314,9 @@ def cfg2_full():
 def cfg2_conv():
     x, y = synthetic.cfg2()
     out = {}
-    for tag, be in (("f32", CPU32), ("f64", CPU64)):
+    # float64 only: the reference's float32 run of this case never reaches tol 1e-6 (its error stalls near 1.4e-5,
+    # the float32 floor), so it would only run to max_iters
+    for tag, be in (("f64", CPU64),):
         t = __import__("time").perf_counter()
         r = ref_sk.sinkhorn(x, y, opts=ref_sk.SinkhornOptions(eps=0.1, tol=1e-6, check_every=10, max_iters=20_000,
                                                              normalize=False, backend=be))
@@ -323,7 +325,7 @@ def cfg2_conv():
         dt = np.float64 if tag == "f64" else np.float32
         out[f"f_{tag}"], out[f"g_{tag}"] = r.f.astype(dt), r.g.astype(dt)
         out[f"meta_{tag}"] = np.array([r.iterations, r.error, float(r.converged)])
-        np.savez_compressed(HERE / "cfg2_conv.npz", **out)      # the float32 run alone is already useful
+        np.savez_compressed(HERE / "cfg2_conv.npz", **out)      # the float64 run alone is already useful
 
 
 def cfg3_full():
