@@ -60,14 +60,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// A waiting thread sleeps in try_wait until the phase completes or kWaitHintNs pass. The producer, bias and MMA
+// warps spend most of their time waiting, on the same sub-partitions as the epilogue warps: every poll is an issue
+// slot taken from the epilogue, so the polls are kept rare (the wake-up on completion does not wait for the hint).
+constexpr uint32_t kWaitHintNs = 20000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n.reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       "selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kWaitHintNs)
       : "memory");
   return ok != 0;
 }
@@ -512,7 +516,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       seg_issued = seg + 1;
       for (; u < seg_end; ++u, ++T) {
-        const int c = (int)(u % sk.nct);
+        const int c = (int)(u - (long long)r * sk.nct);   // (no 64-bit division per tile)
         const int stage = T % C::NS;
         issued_current = false;
         ok = mbar_wait(&empty_b[stage], ((T / C::NS) & 1) ^ 1, abort_flag, p.error_word);
@@ -558,14 +562,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ok = false;
       }
     }
-    for (long long u = u_begin; u < u_end && ok; ++u, ++T) {
-      const int c = (int)(u % sk.nct);
+    // The column tile is tracked, not divided out of u, and whole tiles load without bounds checks: this warp's
+    // instructions share issue slots with the epilogue warps of its sub-partition.
+    int c = (int)(u_begin % sk.nct);
+    for (long long u = u_begin; u < u_end && ok; ++u, ++T, c = (c + 1 == sk.nct) ? 0 : c + 1) {
       float g[TC_BN / 32], l[TC_BN / 32];
+      if ((c + 1) * TC_BN <= p.m) {
 #pragma unroll
-      for (int q = 0; q < TC_BN / 32; ++q) {
-        const int j = c * TC_BN + q * 32 + lane;
-        g[q] = j < p.m ? __ldcg(ghp + j) : 0.f;
-        l[q] = j < p.m ? __ldg(lbp + j) : -INFINITY;
+        for (int q = 0; q < TC_BN / 32; ++q) {
+          const int j = c * TC_BN + q * 32 + lane;
+          g[q] = __ldcg(ghp + j);
+          l[q] = __ldg(lbp + j);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < TC_BN / 32; ++q) {
+          const int j = c * TC_BN + q * 32 + lane;
+          g[q] = j < p.m ? __ldcg(ghp + j) : 0.f;
+          l[q] = j < p.m ? __ldg(lbp + j) : -INFINITY;
+        }
       }
       const int bslot = T % TC_NBB;
       ok = mbar_wait(&bias_empty[bslot], ((T / TC_NBB) & 1) ^ 1, abort_flag, p.error_word);
