@@ -137,6 +137,21 @@ def test_tc_and_ffma_agree_at_config_2_size():
     assert np.abs(a - b).max() / 0.1 <= 2 * HS_TOL
 
 
+@pytest.mark.parametrize("rows", [128, 2000])
+def test_large_column_cloud_in_common_sweep_order(rows):
+    """A column cloud over 32 MB packed (140,001 columns at d 64, a ragged last column tile) is swept by every CTA in
+    a common phase, each row tile starting at its own rotation: one row tile spread over all CTAs (the rotation taken
+    from a CTA more than 31 ranges away) and 16 row tiles of ~9 CTAs each, against the oracle on 64 sampled rows."""
+    m, d, eps = 140_001, 64, 0.05
+    assert m * 2 * d * 2 > 32 << 20
+    x, xsq, off, y, gh, lb = problem(rows, m, d, 11 + rows, eps)
+    fh = gpu_half_step(x, xsq, off, y, gh, lb, eps, 1.0, path=_capi.PATH_TC)
+    pick = np.random.default_rng(rows).choice(rows, 64, replace=False)
+    ref = oracle_half_step(x[pick], xsq[pick], off[pick], y, gh, lb, eps, 1.0)
+    err = np.abs(fh[pick] - ref).max() / eps
+    assert np.all(np.isfinite(fh)) and err <= HS_TOL, err
+
+
 def test_fma_pipe_exp2_against_cuda_exp2f():
     """The FMA-pipe 2^x (range reduction + degree-5 polynomial fitted for this library) against CUDA's exp2f
     (torch.exp2 on the GPU) and against float64: relative error within 3e-7 over [-125, 100]."""

@@ -69,6 +69,7 @@ struct StreamK {
   int parts_per_cta;   // partials one CTA writes per segment (1 for the FFMA kernel, 2 for the tcgen05 kernel)
   int* counters;       // (nrt,) arrival counters, zero between launches
   float2* partials;    // (nrt, slots * parts_per_cta, BM) of (M, l)
+  int rotate = 0;      // tcgen05 kernel: sweep each row tile's column tiles in the CTAs' common phase
 };
 
 __host__ __device__ inline long long sk_unit_begin(long long k, long long units, long long grid) {

@@ -381,6 +381,54 @@ __device__ __forceinline__ uint2 bias_split(float x) {
                     (uint32_t)__bfloat16_as_ushort(h3));
 }
 
+// Column order within a row tile, for column clouds larger than L2 holds comfortably (StreamK::rotate, set by
+// tc_plan). Row tile r visits its column tiles starting at tile (nct - p) mod nct, where p is the column phase (unit
+// index mod nct) at which the row's owner -- the CTA holding its last unit -- begins its range. Every CTA then
+// sweeps the column tiles in step with the others (its tile at local step t is t mod nct, up to its last row), so
+// the column tiles in use at one moment are a narrow window of the column cloud instead of all of it: at 262,144
+// columns (a 67 MB cloud) the DRAM reads of a launch drop from ~50 sweeps of the cloud to ~6. Any per-row rotation
+// covers each column tile once; this one is the same for every CTA that asks, since all of them ask the owner. A
+// CTA needs two values: rows that end inside its range are its own, and only its last row can end in a later
+// CTA's range. Computed once per CTA by a whole warp: lane i takes the range start of CTA blockIdx.x + i and its
+// phase, so the owner is found by a ballot and the start-up path stays two 64-bit divisions deep (the per-tile
+// path has none). Without rotation the order is the natural one.
+struct TcColumnOrder {
+  int phase;              // u_begin mod nct
+  int rot_own, rot_last;  // column tile = (u mod nct + rot) mod nct
+  __device__ __forceinline__ int of_row(long long row_end, long long u_end) const {
+    return row_end <= u_end ? rot_own : rot_last;
+  }
+};
+template <bool kRotate>
+__device__ __forceinline__ TcColumnOrder tc_column_order(const StreamK& sk, long long u_begin, int lane) {
+  TcColumnOrder o;
+  if (!kRotate) {
+    o.phase = (int)(u_begin % sk.nct);
+    o.rot_own = o.rot_last = 0;
+    return o;
+  }
+  const long long k = (long long)blockIdx.x + lane;
+  const long long b = k < sk.grid ? sk_unit_begin(k, sk.units, sk.grid) : sk.units;   // nondecreasing in the lane
+  const int ph = (int)(b % sk.nct);
+  o.phase = __shfl_sync(0xffffffffu, ph, 0);
+  const int ph_end = __shfl_sync(0xffffffffu, ph, 1);   // u_end mod nct (0 when u_end is the last unit + 1)
+  const long long u_end = __shfl_sync(0xffffffffu, b, 1);
+  o.rot_own = o.phase == 0 ? 0 : sk.nct - o.phase;
+  o.rot_last = o.rot_own;
+  if (ph_end != 0) {   // the last row runs past u_end: its owner is the CTA whose range holds its last unit
+    const long long last = u_end - ph_end + sk.nct - 1;
+    const unsigned below = __ballot_sync(0xffffffffu, b <= last);   // lanes 0 .. owner (lane 0 always)
+    int p;
+    if (below != 0xffffffffu) {
+      p = __shfl_sync(0xffffffffu, ph, 31 - __clz(below));
+    } else {   // a row tile over more than 31 CTAs (tiny problems): directly
+      p = (int)(sk_unit_begin(sk_cta_of(last, sk.units, sk.grid), sk.units, sk.grid) % sk.nct);
+    }
+    o.rot_last = p == 0 ? 0 : sk.nct - p;
+  }
+  return o;
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // The kernel
 // ------------------------------------------------------------------------------------------------------------
@@ -410,7 +458,7 @@ struct TcArgs {
   Publish pub;       // world > 1: wait for the other GPUs' rows of gh, publish this GPU's rows of the output
 };
 
-template <int NKB>
+template <int NKB, bool kRotate>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     half_step_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const TcArgs args) {
@@ -503,9 +551,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ---------------------------------------------------------------- producer
     int T = 0, seg = 0, seg_issued = 0;
     bool ok = true, issued_current = false;
+    const TcColumnOrder order = tc_column_order<kRotate>(sk, u_begin, lane);
     for (long long u = u_begin; u < u_end && ok; ++seg) {
       const int r = (int)(u / sk.nct);
-      const long long seg_end = min(u_end, (long long)(r + 1) * sk.nct);
+      const long long row_end = (long long)(r + 1) * sk.nct;
+      const long long seg_end = min(u_end, row_end);
+      const int rot = order.of_row(row_end, u_end);
       const int a_slot = seg & 1;
       ok = mbar_wait(&a_empty[a_slot], ((seg >> 1) & 1) ^ 1, abort_flag, p.error_word);
       if (!ok) break;
@@ -516,7 +567,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       seg_issued = seg + 1;
       for (; u < seg_end; ++u, ++T) {
-        const int c = (int)(u - (long long)r * sk.nct);   // (no 64-bit division per tile)
+        int c = (int)(u - (long long)r * sk.nct) + rot;   // (no 64-bit division per tile)
+        if (kRotate && c >= sk.nct) c -= sk.nct;
         const int stage = T % C::NS;
         issued_current = false;
         ok = mbar_wait(&empty_b[stage], ((T / C::NS) & 1) ^ 1, abort_flag, p.error_word);
@@ -551,6 +603,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const float* __restrict__ ghp = p.gh;
     const float* __restrict__ lbp = p.log_b;
     const float inv_dot2 = 1.0f / dot2_e;
+    // The column tile is tracked, not divided out of u, and whole tiles load without bounds checks: this warp's
+    // instructions share issue slots with the epilogue warps of its sub-partition.
+    const TcColumnOrder order = tc_column_order<kRotate>(sk, u_begin, lane);
+    int cu = order.phase;   // u mod nct
+    long long row_end = u_begin - cu + sk.nct;
+    int rot = order.of_row(row_end, u_end);
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the previous grid (which may write gh) is complete
     int T = 0;
     bool ok = true;
@@ -562,10 +620,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ok = false;
       }
     }
-    // The column tile is tracked, not divided out of u, and whole tiles load without bounds checks: this warp's
-    // instructions share issue slots with the epilogue warps of its sub-partition.
-    int c = (int)(u_begin % sk.nct);
-    for (long long u = u_begin; u < u_end && ok; ++u, ++T, c = (c + 1 == sk.nct) ? 0 : c + 1) {
+    for (long long u = u_begin; u < u_end && ok; ++u, ++T) {
+      int c = cu + rot;
+      if (kRotate && c >= sk.nct) c -= sk.nct;
+      if (++cu == sk.nct) {
+        cu = 0;
+        row_end += sk.nct;
+        rot = order.of_row(row_end, u_end);
+      }
       float g[TC_BN / 32], l[TC_BN / 32];
       if ((c + 1) * TC_BN <= p.m) {
 #pragma unroll
@@ -849,8 +911,10 @@ int g_tc_sms[64] = {0};
 
 }  // namespace
 
+// Column clouds above this size (packed FP16 bytes) are swept in the CTAs' common phase (tc_column_order).
+constexpr long long kTcRotateBytes = 32ll << 20;
+
 void tc_plan(int device, int rows, int m, int d, StreamK& sk) {
-  (void)d;
   if (device < 0 || device >= 64) device = 0;
   if (g_tc_sms[device] == 0) cudaDeviceGetAttribute(&g_tc_sms[device], cudaDevAttrMultiProcessorCount, device);
   sk.nrt = (rows + TC_BM - 1) / TC_BM;
@@ -860,16 +924,18 @@ void tc_plan(int device, int rows, int m, int d, StreamK& sk) {
   sk.grid = (int)(g < sk.units ? g : sk.units);
   sk.slots = 2 * sk_max_slots(sk.units, sk.grid, sk.nct);
   sk.parts_per_cta = 2;
+  sk.rotate = (long long)m * tc_kp(d) * 2 > kTcRotateBytes ? 1 : 0;
 }
 
 size_t tc_partial_bytes(const StreamK& sk) { return (size_t)sk.nrt * sk.slots * TC_BM * sizeof(float2); }
 
-template <int NKB>
+template <int NKB, bool kRotate>
 static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& a, cudaStream_t stream,
                                bool pdl) {
   using C = TcCfg<NKB>;
   static std::atomic<int> attr_done[kMaxDevices];
-  cudaError_t e = smem_attr_once(reinterpret_cast<const void*>(half_step_tc_kernel<NKB>), C::SMEM, attr_done);
+  cudaError_t e =
+      smem_attr_once(reinterpret_cast<const void*>(half_step_tc_kernel<NKB, kRotate>), C::SMEM, attr_done);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.sk.grid);
@@ -881,7 +947,7 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, half_step_tc_kernel<NKB>, ma, mb, a);
+  return cudaLaunchKernelEx(&cfg, half_step_tc_kernel<NKB, kRotate>, ma, mb, a);
 }
 
 cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack, int sx, int sy, const StreamK& sk,
@@ -903,8 +969,11 @@ cudaError_t tc_launch(const LseProblem& p, const void* xpack, const void* ypack,
     a.pub = Publish{};
     a.pub.world = 1;
   }
-  if (kp == 64) return tc_launch_t<1>(ma, mb, a, stream, pdl);
-  return tc_launch_t<2>(ma, mb, a, stream, pdl);
+  // (the rotation is a template choice: the kernel without it carries none of its code)
+  if (kp == 64) {
+    return sk.rotate ? tc_launch_t<1, true>(ma, mb, a, stream, pdl) : tc_launch_t<1, false>(ma, mb, a, stream, pdl);
+  }
+  return sk.rotate ? tc_launch_t<2, true>(ma, mb, a, stream, pdl) : tc_launch_t<2, false>(ma, mb, a, stream, pdl);
 }
 
 }  // namespace trnopt
