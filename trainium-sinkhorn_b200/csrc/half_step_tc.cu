@@ -207,10 +207,28 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __uint_as_float(__float_as_uint(p) + (__float_as_uint(y) << 23));
 }
 
-// 2^x of a pair: on the FMA pipe (ex2_poly) when `poly`, else on MUFU (ex2.approx). (`poly` is a constant once
+// ex2_poly of a pair with packed FP32 operations: per lane the same IEEE operations in the same order (x - r as
+// fma(r, -1, x)), so the same results as two ex2_poly calls, in about half the instructions.
+__device__ __forceinline__ uint64_t ex2_poly2(float x0, float x1) {
+  const uint64_t x = pk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t y = fadd2(x, pk2(12582912.0f, 12582912.0f));
+  const uint64_t f = ffma2(fadd2(y, pk2(-12582912.0f, -12582912.0f)), pk2(-1.0f, -1.0f), x);
+  uint64_t p = ffma2(pk2(0x1.5c08dcp-10f, 0x1.5c08dcp-10f), f, pk2(0x1.3d0c54p-7f, 0x1.3d0c54p-7f));
+  p = ffma2(p, f, pk2(0x1.c6b6e6p-5f, 0x1.c6b6e6p-5f));
+  p = ffma2(p, f, pk2(0x1.ebf918p-3f, 0x1.ebf918p-3f));
+  p = ffma2(p, f, pk2(0x1.62e428p-1f, 0x1.62e428p-1f));
+  p = ffma2(p, f, pk2(0x1.000002p+0f, 0x1.000002p+0f));
+  float p0, p1, y0, y1;
+  upk2(p, p0, p1);
+  upk2(y, y0, y1);
+  return pk2(__uint_as_float(__float_as_uint(p0) + (__float_as_uint(y0) << 23)),
+             __uint_as_float(__float_as_uint(p1) + (__float_as_uint(y1) << 23)));
+}
+
+// 2^x of a pair: on the FMA pipe (ex2_poly2) when `poly`, else on MUFU (ex2.approx). (`poly` is a constant once
 // the callers' loops are unrolled.)
 __device__ __forceinline__ uint64_t ex2_pair(bool poly, float x, float y) {
-  return poly ? pk2(ex2_poly(x), ex2_poly(y)) : pk2(ex2_approx(x), ex2_approx(y));
+  return poly ? ex2_poly2(x, y) : pk2(ex2_approx(x), ex2_approx(y));
 }
 
 // sum_j 2^(a_j - off), four independent packed partial sums. kPoly of every 64 values (spread evenly over the value
@@ -825,7 +843,14 @@ __global__ void tc_pack_kernel(const float* __restrict__ xT, int ldx, int n, int
 }
 
 __global__ void ex2_poly_kernel(const float* __restrict__ x, float* __restrict__ out, int n) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = ex2_poly(x[i]);
+  // (through the packed pair form the fold uses; the second lane checks that both lanes agree)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float a, b;
+    upk2(ex2_poly2(x[i], x[i]), a, b);
+    out[i] = (__float_as_uint(a) == __float_as_uint(b) && __float_as_uint(a) == __float_as_uint(ex2_poly(x[i])))
+                 ? a
+                 : __int_as_float(0x7fc00000);   // NaN: the test sees it
+  }
 }
 
 cudaError_t ex2_poly_launch(const float* x, float* out, int n, cudaStream_t stream) {
