@@ -341,6 +341,16 @@ def peaks():
     return (json.loads(p.read_text()), "measured") if p.exists() else ({}, "fallback")
 
 
+def measured_traffic(path, name, world):
+    """DRAM bytes of one half-step launch from a committed ncu capture of the same kernel and workload
+    (profiles/traffic_<path>_<workload>.json, with an _x<N> suffix for an N-GPU shard), or (None, None)."""
+    tfile = ROOT / "profiles" / (f"traffic_{path}_{name}.json" if world == 1 else f"traffic_{path}_{name}_x{world}.json")
+    if not tfile.exists():
+        return None, None
+    return (json.loads(tfile.read_text()).get("bytes_per_launch"),
+            f"profiles/{tfile.name} (ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch)")
+
+
 def roofline(n, m, d, world, launch_ms, path, clocks, traffic, traffic_src):
     """The north star's roofline of one half-step launch (this GPU's rows of one side against the whole other side):
     the slowest of the exps at the MUFU rate, the useful contraction FLOPs at the pipe's peak and the algorithmic
@@ -578,8 +588,10 @@ def extras_cfg2(world, dev, cpu_ms_cfg2, cpu_on):
     ms5 = statistics.mean(ms)
     d5 = {"workload": "cfg5: 262,144^2, d 64, eps 0.01, one GPU (the N = 1 point of the strong-scaling curve)",
           "ms_per_iter": ms5, "steps": 10, "clocks": clk,
-          "roofline": {k: v for k, v in roofline(len(x5), len(y5), 64, 1, ms5 / 2, sv.path, clk, None, None).items()
-                       if k in ("frac", "bounds_us", "launch_us", "exp_at_sampled_clock")}}
+          "roofline": {k: v for k, v in roofline(len(x5), len(y5), 64, 1, ms5 / 2, sv.path, clk,
+                                                 *measured_traffic(sv.path, "cfg5", 1)).items()
+                       if k in ("frac", "bounds_us", "launch_us", "exp_at_sampled_clock", "traffic", "traffic_source",
+                                "algorithmic_bytes")}}
     del sv
     secs, r = timed_call(solve_cfg5conv(world, dev), world, dev, warm=0)
     d5["staged_solve"] = {"seconds": secs, "iterations": r.iterations,
@@ -625,9 +637,7 @@ def run_ours(args, rank, world, dev):
     step_ms, clocks = sv.timed(args.steps, args.warmup, flush, not args.no_clocks and rank == 0, world)
     ms_per_step = max_over_ranks(sum(step_ms), world, dev) / args.steps
 
-    tfile = ROOT / "profiles" / f"traffic_{sv.path}_{name}.json"
-    traffic = json.loads(tfile.read_text()).get("bytes_per_launch") if tfile.exists() else None
-    tsrc = f"profiles/{tfile.name} (ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch)" if traffic else None
+    traffic, tsrc = measured_traffic(sv.path, name, world)
     launch_ms = statistics.mean(step_ms) / 2          # a step is two launches of the half-step (f then g)
     roof = roofline(len(x), len(y), x.shape[1], world, launch_ms, sv.path, clocks, traffic, tsrc)
     n, m = len(x), len(y)
