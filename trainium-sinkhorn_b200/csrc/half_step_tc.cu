@@ -404,7 +404,7 @@ __device__ __forceinline__ uint2 bias_split(float x) {
 // index mod nct) at which the row's owner -- the CTA holding its last unit -- begins its range. Every CTA then
 // sweeps the column tiles in step with the others (its tile at local step t is t mod nct, up to its last row), so
 // the column tiles in use at one moment are a narrow window of the column cloud instead of all of it: at 262,144
-// columns (a 67 MB cloud) the DRAM reads of a launch drop from ~50 sweeps of the cloud to ~6. Any per-row rotation
+// columns (a 67 MB cloud) the DRAM reads of a launch drop from 6.7 GB (~100 sweeps' worth) to under 1 GB. Any rotation
 // covers each column tile once; this one is the same for every CTA that asks, since all of them ask the owner. A
 // CTA needs two values: rows that end inside its range are its own, and only its last row can end in a later
 // CTA's range. Computed once per CTA by a whole warp: lane i takes the range start of CTA blockIdx.x + i and its
@@ -843,7 +843,7 @@ __global__ void tc_pack_kernel(const float* __restrict__ xT, int ldx, int n, int
 }
 
 __global__ void ex2_poly_kernel(const float* __restrict__ x, float* __restrict__ out, int n) {
-  // (through the packed pair form the fold uses; the second lane checks that both lanes agree)
+  // (through the packed pair form the fold uses; NaN wherever its two lanes or the scalar form disagree)
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     float a, b;
     upk2(ex2_poly2(x[i], x[i]), a, b);
