@@ -106,26 +106,77 @@ __device__ __forceinline__ void lse_merge(float& M, float& l, float M2, float l2
 // way. The weights 2^(M_k - M) <= 1 come from ex2.approx (relative error ~2^-22, the level of the terms inside each
 // partial) and are summed with the partials in double precision, as is the rest of the epilogue. (Double-precision
 // exp2 here, inlined at every merge site, measured 4-7 % slower for the whole tensor-core kernel.)
+// The (max, sum) of K partials held in registers: every load in flight at once, so one L2 round trip.
+template <int K>
+__device__ __forceinline__ void parts_lse(const float2* parts, int nparts, int stride, float& M, double& l) {
+  float2 v[K];
+#pragma unroll
+  for (int s = 0; s < K; ++s) v[s] = s < nparts ? __ldcg(&parts[(size_t)s * stride]) : make_float2(kMaxFloor, 0.f);
+  M = kMaxFloor;
+#pragma unroll
+  for (int s = 0; s < K; ++s) M = fmaxf(M, v[s].x);
+  l = 0.0;
+#pragma unroll
+  for (int s = 0; s < K; ++s)
+    if (v[s].y > 0.f) l += (double)v[s].y * (double)ex2_approx(v[s].x - M);
+}
+
+// More than 8 partials (a row tile spread over more than four CTAs of the tcgen05 kernel: small problems): up to 16
+// in one round of loads, the rest by a loop. Out of line, so the merge sites in the hot loops stay small.
+struct PartsLse {
+  float M;
+  double l;
+};
+static __device__ __noinline__ PartsLse parts_lse_wide(const float2* parts, int nparts, int stride) {
+  constexpr int kW = 16;
+  PartsLse r;
+  parts_lse<kW>(parts, nparts, stride, r.M, r.l);
+  if (nparts > kW) {
+    float M = r.M;
+    for (int s = kW; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
+    double l = r.l * (double)ex2_approx(r.M - M);
+    for (int s = kW; s < nparts; ++s) {
+      const float2 w = __ldcg(&parts[(size_t)s * stride]);
+      if (w.y > 0.f) l += (double)w.y * (double)ex2_approx(w.x - M);
+    }
+    r.M = M;
+    r.l = l;
+  }
+  return r;
+}
+
+// kWide: more than 8 partials go through parts_lse_wide (one round of loads for up to 16); for the merge at the end
+// of a CTA's range, which nothing overlaps. Elsewhere (a merge between tiles, overlapped by the next tiles) they are
+// read by two short loops, which keep those merge sites small.
+template <bool kWide = false>
 __device__ inline float finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride,
                                    double eps, double kappa) {
   constexpr int kRegParts = 8;
   const float xsq = p.mode == 0 ? __ldg(p.xsq + row) : 0.f;
   const float off = (p.mode == 0 && p.off) ? __ldg(p.off + row) : 0.f;
-  float2 v[kRegParts];
+  float M;
+  double l;
+  if (kWide && nparts > kRegParts) {
+    const PartsLse r = parts_lse_wide(parts, nparts, stride);
+    M = r.M;
+    l = r.l;
+  } else {
+    float2 v[kRegParts];
 #pragma unroll
-  for (int s = 0; s < kRegParts; ++s)
-    v[s] = s < nparts ? __ldcg(&parts[(size_t)s * stride]) : make_float2(kMaxFloor, 0.f);
-  float M = kMaxFloor;
+    for (int s = 0; s < kRegParts; ++s)
+      v[s] = s < nparts ? __ldcg(&parts[(size_t)s * stride]) : make_float2(kMaxFloor, 0.f);
+    M = kMaxFloor;
 #pragma unroll
-  for (int s = 0; s < kRegParts; ++s) M = fmaxf(M, v[s].x);
-  for (int s = kRegParts; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
-  double l = 0.0;
+    for (int s = 0; s < kRegParts; ++s) M = fmaxf(M, v[s].x);
+    for (int s = kRegParts; s < nparts; ++s) M = fmaxf(M, __ldcg(&parts[(size_t)s * stride].x));
+    l = 0.0;
 #pragma unroll
-  for (int s = 0; s < kRegParts; ++s)
-    if (v[s].y > 0.f) l += (double)v[s].y * (double)ex2_approx(v[s].x - M);
-  for (int s = kRegParts; s < nparts; ++s) {
-    const float2 w = __ldcg(&parts[(size_t)s * stride]);
-    if (w.y > 0.f) l += (double)w.y * (double)ex2_approx(w.x - M);
+    for (int s = 0; s < kRegParts; ++s)
+      if (v[s].y > 0.f) l += (double)v[s].y * (double)ex2_approx(v[s].x - M);
+    for (int s = kRegParts; s < nparts; ++s) {
+      const float2 w = __ldcg(&parts[(size_t)s * stride]);
+      if (w.y > 0.f) l += (double)w.y * (double)ex2_approx(w.x - M);
+    }
   }
   double lse = ((double)M + log2(l)) * kLn2;
   double res;

@@ -756,7 +756,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // the end of the range), so the atomic's round trip to L2 overlaps the next tile's fold instead of stalling it.
     bool pending = false;
     int pend_old = 0;   // the atomic's result (thread qrow 0)
-#define TRNOPT_RESOLVE_ARRIVAL()                                                                        \
+#define TRNOPT_RESOLVE_ARRIVAL(kWide)                                                                   \
   do {                                                                                                  \
     if (qrow == 0) s_last[wg] = (pend_old == s_pend[2 * wg + 1] - 1);                                   \
     asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");                                         \
@@ -765,7 +765,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int row = pend_r * TC_BM + qrow;                                                            \
       if (row < p.rows) {                                                                               \
         const float2* base = sk.partials + (size_t)pend_r * sk.slots * TC_BM;                           \
-        const float v = finish_row(p, row, base + qrow, pend_expected, TC_BM, eps_e, kappa_e);          \
+        const float v = finish_row<kWide>(p, row, base + qrow, pend_expected, TC_BM, eps_e, kappa_e);   \
         if (args.pub.world > 1) {                                                                       \
           publish_row(args.pub, row, v);                                                                \
           published = true;                                                                             \
@@ -790,7 +790,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             lse_tile128(lane_base + (uint32_t)(acc * TC_BN), dot2, M, L, &acc_empty[acc]);
           }
         }
-        if (pending) TRNOPT_RESOLVE_ARRIVAL();
+        if (pending) TRNOPT_RESOLVE_ARRIVAL(false);
       }
       // Segment done: this warpgroup's partial for row tile r, then one arrival on the row tile's counter.
       const long long first_u = (long long)r * sk.nct;
@@ -807,7 +807,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       pending = true;
     }
-    if (pending) TRNOPT_RESOLVE_ARRIVAL();
+    if (pending) TRNOPT_RESOLVE_ARRIVAL(true);   // the end of the range: nothing to overlap
 #undef TRNOPT_RESOLVE_ARRIVAL
     if (published) __threadfence_system();   // this thread's peer stores, before the CTA barrier below
   }
