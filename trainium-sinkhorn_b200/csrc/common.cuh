@@ -145,9 +145,8 @@ static __device__ __noinline__ PartsLse parts_lse_wide(const float2* parts, int 
   return r;
 }
 
-// kWide: more than 8 partials go through parts_lse_wide (one round of loads for up to 16); for the merge at the end
-// of a CTA's range, which nothing overlaps. Elsewhere (a merge between tiles, overlapped by the next tiles) they are
-// read by two short loops, which keep those merge sites small.
+// kWide: more than 8 partials go through parts_lse_wide (one round of loads for up to 16); for a merge that nothing
+// overlaps (the end of a CTA's range). Otherwise they are read by two short loops, which keep the merge site small.
 template <bool kWide = false>
 __device__ inline float finish_row(const LseProblem& p, int row, const float2* parts, int nparts, int stride,
                                    double eps, double kappa) {
