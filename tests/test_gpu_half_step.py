@@ -91,6 +91,7 @@ def problem(rows, m, d, seed, eps, pad=0):
     (127, 129, 16, 0.1, 0.9, True, 5),
     (128, 128, 64, 0.1, 1.0, False, 0),
     (300, 5000, 30, 0.05, 0.98, True, 200),
+    (1000, 2000, 30, 0.05, 1.0, True, 0),        # d <= 32 kernel, a row tile over 8 CTAs: 16 partials in one round
     (1000, 257, 128, 0.1, 1.0, False, 1),
     (4096, 4096, 64, 0.02, 0.7, True, 96),
     (20000, 700, 64, 0.1, 1.0, False, 0),
